@@ -1,0 +1,424 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 chunked linear cross-entropy hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload lce|ce|sls]
+
+Default workload (``lce``): Llama-3-8B LM head, ``chunked_linear_cross_entropy``
+forward + backward through the public API with H[8192, 4096] (RMS-normalised
+N(0,1)), W[128256, 4096] ~ N(0, 0.02), bf16, 2% ignore_index, mean reduction.
+With N GPUs (torchrun, one process per GPU) every rank runs its own 8192 rows
+(data-parallel, weight replicated, weight gradient all-reduced over NCCL):
+weak scaling, ``value`` = total tokens/s over all ranks.
+
+One JSON line is printed by rank 0. Timing: W warm-up steps, then K steps
+between barrier + synchronize, device time from CUDA events, max over ranks.
+``--workload ce`` / ``sls`` time the standalone row kernels (GB/s).
+``--impl reference`` times the CPU restatement of the reference algorithm
+(the oracle; the reference itself is Python/CuTe-DSL and GPU-only for the
+gradient path) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "linear-CE fwd+bwd tokens/s, Llama-3-8B head; % bf16 TC peak @1/2/4/8 GPU"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# --------------------------------------------------------------------------- dist
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
+            )
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        if not self.path or not os.path.exists(self.path):
+            return out
+        rows = [r.split(",") for r in Path(self.path).read_text().strip().splitlines() if r.strip()]
+        os.unlink(self.path)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if sm:
+            out.update(sm_mhz=statistics.median(sm), sm_max_mhz=max(mx), reasons=sorted(reasons), samples=len(sm))
+        return out
+
+
+# --------------------------------------------------------------------------- workloads
+
+def make_lce_inputs(N, D, V, seed, device, w_std=0.02, ignore_frac=0.02):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    H = torch.randn(N, D, device=device, generator=g)
+    H = H * torch.rsqrt(H.square().mean(-1, keepdim=True) + 1e-6)
+    W = (torch.randn(V, D, device=device, generator=g) * w_std).to(torch.bfloat16)
+    t = torch.randint(0, V, (N,), device=device, generator=g)
+    ign = torch.rand(N, device=device, generator=g) < ignore_frac
+    t[ign] = -100
+    return H.to(torch.bfloat16), W, t
+
+
+def time_steps(step, steps, warmup, world):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(end) / steps
+    return max_over_ranks(ms, world)
+
+
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_baseline_lce(N, D, V, budget_s=12.0, rows_per_sample=64):
+    """Oracle (numpy, fp32 BLAS on all host threads) on row samples of the workload."""
+    import numpy as np
+
+    from oracle import gh_oracle as O
+
+    rng = np.random.default_rng(2)
+    gen = torch.Generator().manual_seed(2)
+    W = (torch.randn(V, D, generator=gen) * 0.02).to(torch.bfloat16).float().numpy()
+    acc = np.zeros((D, V), dtype=np.float32)  # fp32 weight-gradient accumulator, as the reference
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        H = rng.standard_normal((rows_per_sample, D), dtype=np.float32)
+        H = O.round_bf16(H / np.sqrt((H * H).mean(1, keepdims=True) + 1e-6))
+        t = rng.integers(0, V, size=rows_per_sample)
+        O.chunk_step(H, W, t, 0.0, -100, "bf16", acc)
+        done += rows_per_sample
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    el = time.perf_counter() - t0
+    return {
+        "value": done / el,
+        "unit": "tokens/s",
+        "cores": cpu_threads(),
+        "kind": "port",
+        "sample": f"{done} rows of the {N}x{D}x{V} workload in {rows_per_sample}-row chunks of the reference loop (logits, CE+grad, dH, fp32 dW accumulate), {el:.1f}s",
+    }
+
+
+def bench_lce(args, rank, world, local):
+    from greyhound_b200 import _lib
+    from greyhound_b200.nn.functional import chunked_linear_cross_entropy
+
+    N, D, V = 8192, 4096, 128256
+    dev = torch.device("cuda", local)
+    H, W, t = make_lce_inputs(N, D, V, 2 + rank, dev)
+    H.requires_grad_(True)
+    W.requires_grad_(True)
+    if world > 1:
+        from greyhound_b200.distributed import row_sharded_linear_cross_entropy as fn
+    else:
+        fn = chunked_linear_cross_entropy
+
+    def step():
+        H.grad = None
+        W.grad = None
+        loss = fn(H, W, t)
+        loss.backward()
+
+    # device-resident timing
+    c0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, args.warmup, world)
+    launches = (_lib.launch_count() - c0) // (args.steps + args.warmup)
+    clocks = clk.summary()
+
+    # end-to-end: H/targets copied from pinned host memory every step, loss read back
+    H_host = H.detach().cpu().pin_memory()
+    t_host = t.cpu().pin_memory()
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    Hd = torch.empty_like(H.detach())
+    td = torch.empty_like(t)
+
+    def e2e_step():
+        Hd.copy_(H_host, non_blocking=True)
+        td.copy_(t_host, non_blocking=True)
+        Hin = Hd.detach().requires_grad_(True)
+        W.grad = None
+        loss = fn(Hin, W, td)
+        loss.backward()
+        loss_host.copy_(loss.detach(), non_blocking=True)
+
+    ms_e2e = time_steps(e2e_step, args.steps, args.warmup, world)
+
+    peaks, peak_src = load_peaks()
+    flops = 6.0 * N * D * V
+    tflops = flops / (ms * 1e-3) / 1e12
+    value = N * world / (ms * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded randn of the workload's shapes; no dataset)",
+        "config": {
+            "workload": "Llama-3-8B LM head chunked_linear_cross_entropy fwd+bwd (BASELINE configs[2])",
+            "N_per_rank": N, "D": D, "V": V, "global_tokens": N * world,
+            "reduction": "mean", "ignore_frac": 0.02,
+            "parallelism": f"dp{world} (row-sharded, dW all-reduce)" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2 (W = 1.05 GB bf16)",
+        },
+        "tflops_per_gpu": tflops,
+        "frac_of_bf16_peak": tflops / peaks["bf16_tflops"],
+        "roofline": {
+            "bound": "tensor",
+            "kernel": "whole fwd+bwd step (6*N*D*V)",
+            "achieved": tflops,
+            "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s",
+            "frac": tflops / peaks["bf16_tflops"],
+            "peak_source": peak_src,
+            "traffic": None,
+        },
+        "e2e": {
+            "value": N * world / (ms_e2e * 1e-3),
+            "unit": "tokens/s",
+            "ms_per_step": ms_e2e,
+            "h2d_bytes_per_step": H.numel() * 2 + t.numel() * 8,
+            "d2h_bytes_per_step": 4,
+        },
+        "gpu_launches": launches * args.steps,
+        "gpu_launches_per_step": launches,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        del H, W, Hd
+        torch.cuda.empty_cache()
+        line["cpu_baseline"] = cpu_baseline_lce(N, D, V)
+    return line
+
+
+def bench_reference(args, rank, world):
+    """CPU restatement of the reference (the oracle) on the host cores."""
+    if rank != 0:
+        return None
+    N, D, V = 8192, 4096, 128256
+    per_step = []
+    for _ in range(args.warmup + args.steps):
+        b = cpu_baseline_lce(N, D, V, budget_s=args.ref_step_seconds)
+        per_step.append(b)
+    vals = [b["value"] for b in per_step[args.warmup:]]
+    v = statistics.median(vals) if vals else per_step[-1]["value"]
+    cb = dict(per_step[-1])
+    cb["value"] = v
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": v,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * N / v,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 (numpy BLAS on bf16-rounded values)",
+        "data": "synthetic",
+        "config": {"workload": "Llama-3-8B LM head chunked_linear_cross_entropy fwd+bwd (BASELINE configs[2])",
+                   "N_per_rank": N, "D": D, "V": V, "parallelism": "host CPU"},
+        "cpu_baseline": cb,
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def bench_rows(args, rank, world, local, which):
+    """Standalone row kernels: CE+grad on [4096, 128256] (cfg2) or SLS fwd on
+    [65536, 151936] (cfg4), bf16. GB/s with the reference bench formulas."""
+    from greyhound_b200 import _lib
+    from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad
+    from greyhound_b200.kernels.logprobs import selective_log_softmax_with_lse
+
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1 + rank)
+    if which == "ce":
+        rows, V = 4096, 128256
+        x = (torch.randn(rows, V, device=dev, generator=g) * 2).to(torch.bfloat16)
+        t = torch.randint(0, V, (rows,), device=dev, generator=g)
+        out = torch.empty_like(x)
+        step = lambda: cross_entropy_with_grad(x, t, 0.0, -100, out, mean_reduction=True)  # noqa: E731
+        nbytes = 2 * rows * V * 2 + rows * 8
+        metric = "cross_entropy fwd+grad GB/s [4096,128256] bf16"
+    else:
+        rows, V = 65536, 151936
+        x = (torch.randn(rows, V, device=dev, generator=g) * 3).to(torch.bfloat16)
+        t = torch.randint(0, V, (rows,), device=dev, generator=g)
+        step = lambda: selective_log_softmax_with_lse(x, t, out_dtype=torch.float32)  # noqa: E731
+        nbytes = rows * V * 2 + rows * 8 + rows * 4
+        metric = "selective_log_softmax fwd GB/s [65536,151936] bf16"
+    c0 = _lib.launch_count()
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, args.warmup, world)
+    launches = (_lib.launch_count() - c0) // (args.steps + args.warmup)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peaks, src = load_peaks()
+    return {
+        "metric": metric, "value": gbs * world, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": which, "rows": rows, "V": V, "l2": "inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / peaks["hbm_gbs"], "peak_source": src, "traffic": None},
+        "gpu_launches": launches * args.steps, "clocks": clk.summary(),
+    }
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["lce", "ce", "sls"], default="lce")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-step-seconds", type=float, default=8.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = bench_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return 0
+    rank, world, local = dist_setup(args.gpus)
+    if args.workload == "lce":
+        line = bench_lce(args, rank, world, local)
+    else:
+        line = bench_rows(args, rank, world, local, args.workload)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

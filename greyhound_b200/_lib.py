@@ -1,0 +1,127 @@
+"""ctypes binding of the C-ABI library ``_lib/libgreyhound_b200.so``.
+
+Every compute entry point of greyhound_b200 goes through here. There is no
+CPU fallback: if the library is missing or the tensors are not on a CUDA
+device, calls raise. Error codes returned by the library are mapped to the
+exception types the reference raises for the same conditions
+(src/greyhound/kernels/cross_entropy.py:173-184: ValueError for shapes,
+devices and layouts, TypeError for dtypes).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgreyhound_b200.so"
+
+GH_F16, GH_BF16, GH_F32, GH_I32, GH_I64 = 0, 1, 2, 3, 4
+GH_OK, GH_EINVAL, GH_ETYPE, GH_ECUDA, GH_EWORKSPACE, GH_EUNSUPPORTED = 0, 1, 2, 3, 4, 5
+GH_DEV_BAD_LABEL = 1
+
+DTYPE_CODE = {
+    torch.float16: GH_F16,
+    torch.bfloat16: GH_BF16,
+    torch.float32: GH_F32,
+    torch.int32: GH_I32,
+    torch.int64: GH_I64,
+}
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/greyhound_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "gh_abi_version": (_i32, []),
+    "gh_last_error_string": (ctypes.c_char_p, []),
+    "gh_launch_count": (ctypes.c_longlong, []),
+    "gh_workspace_status_offset": (_sz, []),
+    "gh_ce_workspace_bytes": (_sz, [_i64, _i64, _i32]),
+    "gh_ce_fwd_grad": (
+        _i32,
+        [_vp, _vp, _vp, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    ),
+    "gh_sls_workspace_bytes": (_sz, [_i64, _i64, _i32]),
+    "gh_sls_fwd": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _vp, _i32, _vp, _vp, _sz, _vp]),
+    "gh_sls_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i64, _i64, _i32, _vp, _vp]),
+    "gh_logits_grad": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i64, _i64, _vp, _vp]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+class GreyhoundLibraryError(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the C-ABI library. Raises if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise GreyhoundLibraryError(
+                    f"greyhound_b200 CUDA library not found at {LIB_PATH}; build it with "
+                    "`python -m greyhound_b200.build` (there is no CPU fallback)"
+                )
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().gh_last_error_string()
+    return msg.decode() if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status == GH_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if status == GH_EINVAL:
+        raise ValueError(msg)
+    if status == GH_ETYPE:
+        raise TypeError(msg)
+    raise GreyhoundLibraryError(msg)
+
+
+def launch_count() -> int:
+    return int(load().gh_launch_count())
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype: {dtype}") from None
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def device_status(ws: torch.Tensor) -> int:
+    """Read the device status word of a workspace (synchronises the stream)."""
+    off = int(load().gh_workspace_status_offset())
+    return int(ws[off : off + 4].view(torch.int32).item())

@@ -1,0 +1,187 @@
+"""Chunked linear cross-entropy forward+backward on the device.
+
+Computes, for ``logits = inputs @ weight`` (``weight`` given as the ``[D, V]``
+view the ops layer passes, src/greyhound/nn/functional.py:279):
+``ce_sum``, ``z_sum``, ``n_valid``, ``grad_input = dlogits @ weight.T`` and
+``grad_weight = inputs.T @ dlogits`` with
+``dlogits = softmax(logits) * (1 + 2 z lse) - onehot(target)`` (0 on ignored rows),
+following the chunk loop of src/greyhound/ops/chunked_linear_loss.py:56-103 and the
+callback of src/greyhound/ops/chunked_linear_cross_entropy.py:43-59.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad
+
+__all__ = ["linear_cross_entropy_with_grad", "linear_cross_entropy_loss", "chunk_size_for"]
+
+_TARGET_LOGITS_CHUNK_BYTES = 512 * 1024 * 1024
+_LARGE_D_MODEL_TARGET_LOGITS_CHUNK_BYTES = 2 * 1024 * 1024 * 1024
+
+
+def _next_power_of_2(n: int) -> int:
+    return 1 << (n - 1).bit_length()
+
+
+def _prev_power_of_2(n: int) -> int:
+    return 1 << (n.bit_length() - 1)
+
+
+def chunk_size_for(B: int, D: int, V: int, element_size: int) -> int:
+    """Rows per logits chunk: the reference heuristic, ops/chunked_linear_loss.py:24-34.
+
+    ``max(next_pow2(ceil(B / ceil(V / D))), min(B, prev_pow2(T // (V * elt))))``
+    with ``T`` = 2 GiB when ``D >= 4096`` else 512 MiB.
+    """
+    base = _next_power_of_2(-(-B // max(-(-V // D), 1)))
+    base = min(max(base, 1), B)
+    target = _LARGE_D_MODEL_TARGET_LOGITS_CHUNK_BYTES if D >= 4096 else _TARGET_LOGITS_CHUNK_BYTES
+    max_rows = max(target // max(V * element_size, 1), 1)
+    return max(base, min(B, _prev_power_of_2(max_rows)))
+
+
+def _check(inputs: Tensor, weight: Tensor, target: Tensor) -> None:
+    if inputs.ndim != 2 or weight.ndim != 2 or inputs.shape[1] != weight.shape[0]:
+        raise ValueError(
+            f"expected inputs [B, D] and weight [D, V], got {tuple(inputs.shape)} and {tuple(weight.shape)}"
+        )
+    if target.shape != (inputs.shape[0],):
+        raise ValueError(f"expected target shape {(inputs.shape[0],)}, got {tuple(target.shape)}")
+    if not inputs.is_cuda or weight.device != inputs.device or target.device != inputs.device:
+        raise ValueError("expected inputs, weight and target on the same CUDA device")
+
+
+def linear_cross_entropy_with_grad(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    fp32_grad_weight_accum: bool,
+    ignore_index: int,
+    mean_reduction: bool = False,
+    grad_scale: Tensor | None = None,
+    grad_weight_hook=None,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns ``(ce_sum, z_sum, n_valid, grad_input [B, D], grad_weight [D, V])``.
+
+    With ``mean_reduction`` both gradients are already divided by
+    ``max(n_valid, 1)``; ``grad_scale`` (1-element fp32 device tensor)
+    multiplies them further. ``grad_weight_hook(grad_weight)`` runs as soon as
+    the final weight gradient exists (the data-parallel all-reduce hooks in here).
+    """
+    _check(inputs, weight, target)
+    B, D = inputs.shape
+    V = weight.shape[1]
+    chunk = chunk_size_for(B, D, V, inputs.element_size())
+    dev = inputs.device
+    target = target.contiguous()
+    ce_sum = torch.zeros((), dtype=torch.float32, device=dev)
+    z_sum = torch.zeros((), dtype=torch.float32, device=dev)
+    n_valid = torch.zeros((), dtype=torch.float32, device=dev)
+    grad_input = torch.empty_like(inputs)
+    acc_dtype = torch.float32 if fp32_grad_weight_accum else weight.dtype
+    grad_weight_acc = torch.zeros((D, V), dtype=acc_dtype, device=dev)
+    scale = grad_scale.reshape(1).float() if grad_scale is not None else None
+    if mean_reduction:
+        m = 1.0 / (target != ignore_index).sum().float().clamp(min=1.0).reshape(1)
+        scale = m if scale is None else scale * m
+    for s in range(0, B, chunk):
+        e = min(s + chunk, B)
+        x = inputs[s:e]
+        logits = x @ weight
+        c, z, n = cross_entropy_with_grad(
+            logits, target[s:e], z_loss_multiplier, ignore_index, logits, grad_scale=scale
+        )
+        ce_sum += c
+        z_sum += z
+        n_valid += n
+        grad_input[s:e] = logits @ weight.T
+        torch.addmm(grad_weight_acc, x.T, logits, out=grad_weight_acc, out_dtype=acc_dtype)
+    grad_weight = grad_weight_acc.to(weight.dtype)
+    if grad_weight_hook is not None:
+        grad_weight_hook(grad_weight)
+    return ce_sum, z_sum, n_valid, grad_input, grad_weight
+
+
+def linear_cross_entropy_loss(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    ignore_index: int,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """Forward only: ``(ce_sum, z_sum, n_valid)``, no gradient buffers."""
+    _check(inputs, weight, target)
+    B, D = inputs.shape
+    V = weight.shape[1]
+    chunk = chunk_size_for(B, D, V, inputs.element_size())
+    dev = inputs.device
+    target = target.contiguous()
+    ce_sum = torch.zeros((), dtype=torch.float32, device=dev)
+    z_sum = torch.zeros((), dtype=torch.float32, device=dev)
+    n_valid = torch.zeros((), dtype=torch.float32, device=dev)
+    for s in range(0, B, chunk):
+        e = min(s + chunk, B)
+        logits = inputs[s:e] @ weight
+        c, z, n = cross_entropy_with_grad(logits, target[s:e], z_loss_multiplier, ignore_index, None)
+        ce_sum += c
+        z_sum += z
+        n_valid += n
+    return ce_sum, z_sum, n_valid
+
+
+def vocab_shard_stats(inputs: Tensor, weight_shard: Tensor, local_target: Tensor) -> tuple[Tensor, Tensor]:
+    """Per-row statistics of one vocab shard: ``[rows, 3]`` fp32 (m, s, target logit).
+
+    Returned as ``(lse_local, 1, x_t)`` — an exact (max, sum) pair since
+    ``s * exp(m) = exp(lse_local)`` — with ``x_t = -inf`` when the row's target
+    is not in this shard. Also returns the shard's logits ``[rows, V_local]``
+    (kept for the gradient pass).
+    """
+    from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad as _ce
+
+    rows = inputs.shape[0]
+    Vl = weight_shard.shape[0]
+    logits = inputs @ weight_shard.T
+    lse = torch.empty(rows, dtype=torch.float32, device=inputs.device)
+    never = torch.full_like(local_target, -(1 << 62))
+    _ce(logits, never, 0.0, -(1 << 62), None, lse_out=lse)
+    inside = (local_target >= 0) & (local_target < Vl)
+    xt = logits.gather(1, local_target.clamp(0, Vl - 1)[:, None])[:, 0].float()
+    xt = torch.where(inside, xt, torch.full_like(xt, float("-inf")))
+    stats = torch.stack([lse, torch.ones_like(lse), xt], dim=1)
+    return stats, logits
+
+
+def vocab_shard_grads(
+    inputs: Tensor,
+    weight_shard: Tensor,
+    logits: Tensor,
+    local_target: Tensor,
+    lse: Tensor,
+    valid: Tensor,
+    z_loss_multiplier: float,
+    scale: Tensor,
+) -> tuple[Tensor, Tensor]:
+    """Gradient pass of one vocab shard given the global per-row logsumexp.
+
+    Writes the shard's logits gradient in place, then returns the partial
+    ``grad_input`` (to be summed over shards) and the shard's ``grad_weight [V_local, D]``.
+    """
+    from greyhound_b200 import _lib
+
+    rows, Vl = logits.shape
+    labels = torch.where(valid, local_target, torch.full_like(local_target, -(1 << 62)))
+    lib = _lib.load()
+    st = lib.gh_logits_grad(
+        logits.data_ptr(), logits.data_ptr(), labels.data_ptr(), lse.contiguous().data_ptr(),
+        rows, Vl, _lib.dtype_code(logits.dtype), float(z_loss_multiplier), -(1 << 62), 0,
+        scale.reshape(1).float().data_ptr(), _lib.stream_of(logits),
+    )
+    _lib.check(st, "gh_logits_grad")
+    grad_input = logits @ weight_shard
+    grad_weight = (logits.T @ inputs)
+    return grad_input, grad_weight

@@ -1,0 +1,172 @@
+"""Chunked linear cross-entropy custom op + autograd Function.
+
+Mirrors src/greyhound/ops/chunked_linear_cross_entropy.py: the op
+``greyhound::chunked_linear_cross_entropy_fwd(inputs[B,D], weight[D,V], target[B],
+z_loss_multiplier, fp32_grad_weight_accum, ignore_index=-100)
+-> (ce_sum, z_sum, n_valid, grad_input[B,D], grad_weight[D,V])`` (:19-67) with
+its fake (:70-88), the forward-only fast path (:91-132) and
+``ChunkedLinearCrossEntropyFunction`` (:135-185), including the
+``ctx.needs_input_grad`` gate (:150) and gradients computed in the forward and
+scaled by ``grad_output`` in the backward.
+
+B200 difference (results unchanged within tolerance): for ``reduction="mean"``
+the Function calls ``greyhound::chunked_linear_cross_entropy_fwd_mean``, which
+folds ``1 / max(n_valid, 1)`` into the logits gradient before the two
+gradient GEMMs instead of two ``mul_`` passes over ``grad_input`` and
+``grad_weight`` afterwards (:159-164).
+"""
+
+from __future__ import annotations
+
+from typing import Literal
+
+import torch
+from torch import Tensor
+
+from greyhound_b200.kernels.linear_cross_entropy import (
+    linear_cross_entropy_loss,
+    linear_cross_entropy_with_grad,
+)
+
+__all__ = [
+    "ChunkedLinearCrossEntropyFunction",
+    "chunked_linear_cross_entropy_fwd",
+    "chunked_linear_cross_entropy_fwd_mean",
+]
+
+
+def _fake(inputs: Tensor, weight: Tensor) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    B, D = inputs.shape
+    V = weight.shape[1]
+    return (
+        torch.empty([], dtype=torch.float32, device=inputs.device),
+        torch.empty([], dtype=torch.float32, device=inputs.device),
+        torch.empty([], dtype=torch.float32, device=inputs.device),
+        torch.empty([B, D], dtype=inputs.dtype, device=inputs.device),
+        torch.empty([D, V], dtype=weight.dtype, device=inputs.device),
+    )
+
+
+@torch.library.custom_op("greyhound::chunked_linear_cross_entropy_fwd", mutates_args=())
+def chunked_linear_cross_entropy_fwd(
+    inputs: Tensor,  # [B, D]
+    weight: Tensor,  # [D, V]
+    target: Tensor,  # [B]
+    z_loss_multiplier: float,
+    fp32_grad_weight_accum: bool,
+    ignore_index: int = -100,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Returns (ce_sum, z_sum, n_valid, grad_input, grad_weight) of the summed loss."""
+    return linear_cross_entropy_with_grad(
+        inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index
+    )
+
+
+@chunked_linear_cross_entropy_fwd.register_fake
+def _(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    fp32_grad_weight_accum: bool,
+    ignore_index: int = -100,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    return _fake(inputs, weight)
+
+
+@torch.library.custom_op("greyhound::chunked_linear_cross_entropy_fwd_mean", mutates_args=())
+def chunked_linear_cross_entropy_fwd_mean(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    fp32_grad_weight_accum: bool,
+    ignore_index: int = -100,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """As ``chunked_linear_cross_entropy_fwd`` with gradients divided by max(n_valid, 1)."""
+    return linear_cross_entropy_with_grad(
+        inputs,
+        weight,
+        target,
+        z_loss_multiplier,
+        fp32_grad_weight_accum,
+        ignore_index,
+        mean_reduction=True,
+    )
+
+
+@chunked_linear_cross_entropy_fwd_mean.register_fake
+def _(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    fp32_grad_weight_accum: bool,
+    ignore_index: int = -100,
+) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    return _fake(inputs, weight)
+
+
+def _forward_only_chunked_ce(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    ignore_index: int,
+    reduction: str,
+    z_loss_multiplier: float,
+) -> Tensor:
+    """Forward-only path (no gradient buffers), ops/chunked_linear_cross_entropy.py:91-132."""
+    ce_sum, z_sum, n_valid = linear_cross_entropy_loss(
+        inputs, weight, target, z_loss_multiplier, ignore_index
+    )
+    loss = ce_sum + z_loss_multiplier * z_sum
+    if reduction == "mean":
+        loss = loss / n_valid.clamp(min=1.0)
+    return loss
+
+
+class ChunkedLinearCrossEntropyFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(
+        ctx: object,
+        inputs: Tensor,  # [B, D]
+        weight: Tensor,  # [D, V]
+        target: Tensor,  # [B]
+        ignore_index: int = -100,
+        reduction: Literal["sum", "mean"] = "mean",
+        z_loss_multiplier: float = 0.0,
+        fp32_grad_weight_accum: bool = True,
+    ) -> Tensor:
+        # torch.is_grad_enabled() is always False inside Function.forward; gate on
+        # needs_input_grad exactly like the reference (:150).
+        if not ctx.needs_input_grad[0] and not ctx.needs_input_grad[1]:  # type: ignore[attr-defined]
+            return _forward_only_chunked_ce(
+                inputs, weight, target, ignore_index, reduction, z_loss_multiplier
+            )
+        if reduction == "mean":
+            ce_sum, z_sum, n_valid, grad_input, grad_weight = chunked_linear_cross_entropy_fwd_mean(
+                inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index
+            )
+            loss = (ce_sum + z_loss_multiplier * z_sum) / n_valid.clamp(min=1.0)
+        elif reduction == "sum":
+            ce_sum, z_sum, n_valid, grad_input, grad_weight = chunked_linear_cross_entropy_fwd(
+                inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index
+            )
+            loss = ce_sum + z_loss_multiplier * z_sum
+        else:
+            raise ValueError(f"Unsupported reduction: {reduction}")
+        ctx.save_for_backward(grad_input, grad_weight, n_valid)  # type: ignore[attr-defined]
+        return loss
+
+    @staticmethod
+    def backward(ctx: object, grad_output: Tensor):  # type: ignore[override]
+        grad_input, grad_weight, _ = ctx.saved_tensors  # type: ignore[attr-defined]
+        return (
+            grad_input * grad_output,
+            grad_weight * grad_output,
+            None,
+            None,
+            None,
+            None,
+            None,
+        )

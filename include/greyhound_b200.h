@@ -1,0 +1,139 @@
+/*
+ * greyhound_b200 — C-ABI of the B200 (sm_100a) replacement for greyhound's
+ * chunked linear cross-entropy hot path and the two row kernels that share
+ * its reduction core.
+ *
+ * Conventions for every entry point:
+ *   - pointers are DEVICE pointers unless stated otherwise; tensors are dense
+ *     and row-major (C-contiguous), exactly the layouts the reference demands
+ *     (src/greyhound/kernels/cross_entropy.py:183, kernels/logprobs.py:152);
+ *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream);
+ *     every call only enqueues work on it and never synchronises the host;
+ *   - the return value is GH_OK or an error code; gh_last_error_string()
+ *     gives a human-readable message for the last failure on this host thread;
+ *   - the library never allocates device memory: scratch space is passed in
+ *     by the caller (`workspace`, sized by the matching *_workspace_bytes);
+ *   - device-side problems (e.g. a label outside [0, V)) never trap: they are
+ *     recorded in the workspace status word, see gh_workspace_status_offset().
+ */
+#ifndef GREYHOUND_B200_H
+#define GREYHOUND_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GH_API __attribute__((visibility("default")))
+#else
+#define GH_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes (logits / hidden / weight / index / output element types) */
+enum {
+  GH_F16 = 0,
+  GH_BF16 = 1,
+  GH_F32 = 2,
+  GH_I32 = 3,
+  GH_I64 = 4
+};
+
+/* status codes; the Python layer maps EINVAL->ValueError, ETYPE->TypeError,
+ * everything else -> RuntimeError (mirrors kernels/cross_entropy.py:173-184) */
+enum {
+  GH_OK = 0,
+  GH_EINVAL = 1,
+  GH_ETYPE = 2,
+  GH_ECUDA = 3,
+  GH_EWORKSPACE = 4,
+  GH_EUNSUPPORTED = 5
+};
+
+/* device-side status bits written into the workspace status word */
+enum {
+  GH_DEV_BAD_LABEL = 1   /* a non-ignored label/index outside [0, V) */
+};
+
+GH_API int gh_abi_version(void);
+GH_API const char* gh_last_error_string(void);
+/* Number of kernels this library has launched in this process (all devices). */
+GH_API long long gh_launch_count(void);
+/* Byte offset of the int32 device status word inside any workspace. */
+GH_API size_t gh_workspace_status_offset(void);
+
+/* ------------------------------------------------------------------------ *
+ * Standalone cross-entropy with logits gradient.
+ * Replaces cross_entropy_with_grad_kernel(logits, labels, z_loss_multiplier,
+ * ignore_index) -> (ce_sum, z_sum, n_valid)       kernels/cross_entropy.py:166
+ * and the op around it                           ops/cross_entropy.py:11-26.
+ *
+ *   logits  [rows, vocab] dtype in {F16, BF16, F32}
+ *   dlogits [rows, vocab] same dtype; may equal `logits` (in place, as the
+ *           reference kernel does) or be NULL (loss only, no gradient)
+ *   labels  [rows] int64; `ignore_index` rows contribute nothing and get a
+ *           zero gradient row
+ *   ce_sum, z_sum, n_valid: float scalars, overwritten (not added to)
+ *   lse_out optional float[rows] <- natural-log logsumexp of each row
+ *   mean_reduction: 0 -> gradient of the SUM (reference op semantics);
+ *                   1 -> gradient already divided by max(n_valid, 1), i.e. the
+ *                   mean scaling of ops/cross_entropy.py:63-66 fused in.
+ *   grad_scale      optional device float; when given the gradient is also
+ *                   multiplied by *grad_scale (e.g. 1/global_n_valid computed
+ *                   on the device by a data-parallel caller)
+ * Gradient: softmax * (1 + 2 z lse) - onehot(label)   kernels/cross_entropy.py:94-108
+ * Loss sums are reduced deterministically (fixed order, no float atomics).
+ * ------------------------------------------------------------------------ */
+GH_API size_t gh_ce_workspace_bytes(int64_t rows, int64_t vocab, int dtype);
+GH_API int gh_ce_fwd_grad(const void* logits, void* dlogits, const int64_t* labels,
+                   int64_t rows, int64_t vocab, int dtype,
+                   float z_loss_multiplier, int64_t ignore_index,
+                   int mean_reduction, const float* grad_scale,
+                   float* ce_sum, float* z_sum, float* n_valid, float* lse_out,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Selective log-softmax: out[r] = logits[r, index[r]] - logsumexp(logits[r]).
+ * Replaces selective_log_softmax_kernel(logits, index)  kernels/logprobs.py:131
+ *   index dtype in {I32, I64}; out dtype in {F16, BF16, F32} (the reference
+ *   writes the logits dtype, kernels/logprobs.py:158); lse_out optional.
+ * ------------------------------------------------------------------------ */
+GH_API size_t gh_sls_workspace_bytes(int64_t rows, int64_t vocab, int dtype);
+GH_API int gh_sls_fwd(const void* logits, const void* index, int index_dtype,
+               int64_t rows, int64_t vocab, int dtype,
+               void* out, int out_dtype, float* lse_out,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward of selective log-softmax (the reference raises NotImplementedError,
+ * ops/logprobs.py:30; this is the autograd derivative of
+ * gather(log_softmax(logits), index)):
+ *   grad_logits[r, v] = grad_out[r] * ([v == index[r]] - exp(logits[r, v] - lse[r]))
+ * lse comes from gh_sls_fwd's lse_out. grad_out dtype in {F16, BF16, F32}. */
+GH_API int gh_sls_bwd(const void* logits, const void* index, int index_dtype,
+               const float* lse, const void* grad_out, int grad_dtype,
+               int64_t rows, int64_t vocab, int dtype, void* grad_logits,
+               void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Logits gradient from a known per-row logsumexp (no reduction):
+ *   dlogits[r, v] = exp(logits[r, v] - lse[r]) * (1 + 2 z lse[r]) * s
+ *                   - s * [v == labels[r] - label_offset]
+ * with s = *grad_scale (1 if NULL); rows with labels[r] == ignore_index get 0.
+ * A label outside [label_offset, label_offset + vocab) only contributes the
+ * softmax term (vocab-sharded use). dlogits may equal logits.
+ * This is the second half of the reference kernel (kernels/cross_entropy.py:94-108)
+ * split out so the statistics can come from a fused GEMM epilogue or from
+ * other vocab shards.
+ * ------------------------------------------------------------------------ */
+GH_API int gh_logits_grad(const void* logits, void* dlogits, const int64_t* labels,
+                          const float* lse, int64_t rows, int64_t vocab, int dtype,
+                          float z_loss_multiplier, int64_t ignore_index,
+                          int64_t label_offset, const float* grad_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GREYHOUND_B200_H */

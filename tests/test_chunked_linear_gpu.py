@@ -1,0 +1,244 @@
+"""Chunked linear cross-entropy / generic chunked linear loss on the GPU.
+
+Restates src/tests/nn/functional/chunked_linear_loss_test.py (same shapes,
+chunk size 11, tolerances) and adds parity with the CPU oracle and the golden
+fixtures made from the reference's own chunk loop."""
+
+from typing import Literal, cast
+
+import numpy as np
+import pytest
+import torch
+from torch import Tensor
+from torch.library import opcheck
+
+from greyhound_b200.nn.functional import (
+    autograd_loss_and_logits_grad,
+    chunked_linear_cross_entropy,
+    chunked_linear_loss,
+)
+from greyhound_b200.ops.chunked_linear_cross_entropy import (
+    chunked_linear_cross_entropy_fwd,
+    chunked_linear_cross_entropy_fwd_mean,
+)
+from greyhound_b200.testing import requires_gpu
+from greyhound_b200.utils import get_default_device
+from oracle import gh_oracle as O
+
+
+def reference_linear_cross_entropy(inputs, weight, target, ignore_index=-100, reduction="mean", z_loss_multiplier=0.0):
+    # weight is [D, V]; ignored rows are masked out of the z-loss (the kernel's
+    # semantics, src/greyhound/kernels/cross_entropy.py:87-92)
+    logits = inputs @ weight
+    ce_loss = torch.nn.functional.cross_entropy(logits.float(), target, ignore_index=ignore_index, reduction=reduction)
+    if z_loss_multiplier > 0.0:
+        valid = target != ignore_index
+        lse = torch.logsumexp(logits.float(), dim=-1)
+        z = (lse.square() * valid).sum()
+        if reduction == "mean":
+            z = z / valid.sum().clamp(min=1)
+        return ce_loss + z_loss_multiplier * z
+    return ce_loss
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+@requires_gpu
+@pytest.mark.parametrize(
+    ("loss_name", "grad_weight_accum_dtype"),
+    [("cross_entropy", "fp32"), ("mse_loss", "fp32"), ("mse_loss", "weight"),
+     ("smooth_l1_loss", "fp32"), ("custom_weighted_mean_square_direct_grad", "fp32")],
+)
+def test_chunked_linear_loss_with_various_loss_functions(loss_name, grad_weight_accum_dtype):
+    device = get_default_device()
+    B, D, V = 37, 64, 257
+    inputs = torch.randn(B, D, device=device, dtype=torch.bfloat16, requires_grad=True)
+    weight = torch.randn(V, D, device=device, dtype=torch.bfloat16, requires_grad=True)
+    inputs_ref = inputs.detach().clone().requires_grad_(True)
+    weight_ref = weight.detach().clone().requires_grad_(True)
+    logits_ref = (inputs_ref @ weight_ref.T).float()
+    kw = {"chunk_size": 11, "grad_weight_accum_dtype": grad_weight_accum_dtype}
+    if loss_name == "cross_entropy":
+        t = torch.randint(0, V, (B,), device=device)
+        result = chunked_linear_loss(inputs, weight, autograd_loss_and_logits_grad(torch.nn.functional.cross_entropy), t, reduction="sum", **kw)
+        expected = torch.nn.functional.cross_entropy(logits_ref, t, reduction="sum")
+    elif loss_name == "mse_loss":
+        t = torch.randn(B, V, device=device)
+        f = lambda lg, tt, reduction: torch.nn.functional.mse_loss(lg.float(), tt, reduction=reduction)  # noqa: E731
+        result = chunked_linear_loss(inputs, weight, autograd_loss_and_logits_grad(f), t, reduction="sum", **kw)
+        expected = f(logits_ref, t, reduction="sum")
+    elif loss_name == "smooth_l1_loss":
+        t = torch.randn(B, V, device=device)
+        result = chunked_linear_loss(inputs, weight, autograd_loss_and_logits_grad(torch.nn.functional.smooth_l1_loss), target=t, reduction="sum", beta=0.25, **kw)
+        expected = torch.nn.functional.smooth_l1_loss(logits_ref, target=t, reduction="sum", beta=0.25)
+    else:
+        t = torch.randn(B, V, device=device)
+        rw = torch.rand(B, device=device) + 0.5
+        fw = torch.rand(V, device=device) + 0.5
+
+        def lg(logits, target, row_weight, feature_weight, scale):
+            err = logits.float() - target
+            w = row_weight[:, None] * feature_weight[None, :]
+            return scale * (err.square() * w).sum(), (2 * scale * err * w).to(logits.dtype)
+
+        result = chunked_linear_loss(inputs, weight, lg, t, rw, fw, scale=0.125, **kw)
+        expected = 0.125 * ((logits_ref - t).square() * rw[:, None] * fw[None, :]).sum()
+    tol = 5e-2 if grad_weight_accum_dtype == "fp32" else 8e-2
+    assert torch.allclose(result.float(), expected.float(), rtol=5e-3, atol=5e-3)
+    result.backward()
+    expected.backward()
+    assert _rel(inputs.grad, inputs_ref.grad) < tol
+    assert _rel(weight.grad, weight_ref.grad) < tol
+
+
+@requires_gpu
+@pytest.mark.parametrize("reduction", ["mean", "sum"])
+@pytest.mark.parametrize("ignore_index", [None, -100])
+@pytest.mark.parametrize("z_loss_multiplier", [0.0, 1e-4])
+def test_chunked_linear_cross_entropy_correctness(reduction, ignore_index, z_loss_multiplier):
+    device = get_default_device()
+    B, D, V = 32, 128, 1000
+    inputs = torch.randn(B, D, device=device, dtype=torch.bfloat16)
+    weight = torch.randn(V, D, device=device, dtype=torch.bfloat16)
+    target = torch.randint(0, V, (B,), device=device)
+    if ignore_index is not None:
+        target[::4] = ignore_index
+    ii = ignore_index if ignore_index is not None else -100
+    result = chunked_linear_cross_entropy(inputs, weight, target, ignore_index=ii, reduction=reduction, z_loss_multiplier=z_loss_multiplier)
+    expected = reference_linear_cross_entropy(inputs, weight.T, target, ignore_index=ii, reduction=reduction, z_loss_multiplier=z_loss_multiplier)
+    assert torch.allclose(result.float(), expected.float(), rtol=5e-3, atol=5e-3)
+
+
+@requires_gpu
+@pytest.mark.parametrize("z_loss_multiplier", [0.0, 1e-4])
+@pytest.mark.parametrize("reduction", ["sum", "mean"])
+def test_chunked_linear_cross_entropy_gradient_correctness(reduction, z_loss_multiplier):
+    device = get_default_device()
+    B, D, V = 32, 128, 1000
+    inputs = torch.randn(B, D, device=device, dtype=torch.bfloat16, requires_grad=True)
+    weight = torch.randn(V, D, device=device, dtype=torch.bfloat16, requires_grad=True)
+    target = torch.randint(0, V, (B,), device=device)
+    inputs_ref = inputs.clone().detach().requires_grad_(True)
+    weight_ref = weight.clone().detach().requires_grad_(True)
+    result = chunked_linear_cross_entropy(inputs, weight, target, reduction=cast(Literal["sum", "mean"], reduction), z_loss_multiplier=z_loss_multiplier)
+    expected = reference_linear_cross_entropy(inputs_ref, weight_ref.T, target, reduction=reduction, z_loss_multiplier=z_loss_multiplier)
+    result.backward()
+    expected.backward()
+    assert _rel(inputs.grad, inputs_ref.grad) < 5e-2
+    assert _rel(weight.grad, weight_ref.grad) < 5e-2
+
+
+@requires_gpu
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_chunked_linear_cross_entropy_fwd_opcheck(dtype):
+    device = get_default_device()
+    for B, D, V in [(16, 64, 256), (32, 128, 1000), (64, 256, 2000)]:
+        inputs = torch.randn(B, D, device=device, dtype=dtype)
+        weight = torch.randn(D, V, device=device, dtype=dtype)
+        target = torch.randint(0, V, (B,), device=device)
+        opcheck(chunked_linear_cross_entropy_fwd, (inputs, weight, target, 0.0, True, -100), raise_exception=True)
+        opcheck(chunked_linear_cross_entropy_fwd, (inputs, weight, target, 1e-4, True, -100), raise_exception=True)
+        opcheck(chunked_linear_cross_entropy_fwd, (inputs, weight, target, 0.0, False, -100), raise_exception=True)
+        opcheck(chunked_linear_cross_entropy_fwd_mean, (inputs, weight, target, 1e-4, True, -100), raise_exception=True)
+
+
+@requires_gpu
+@pytest.mark.parametrize("z_loss_multiplier", [0.0, 1e-4])
+def test_chunked_linear_cross_entropy_compile(z_loss_multiplier):
+    device = get_default_device()
+    B, D, V = 32, 128, 1000
+
+    @torch.compile(fullgraph=True)
+    def compiled_fn(inputs, weight, target):
+        return chunked_linear_cross_entropy(inputs, weight, target, z_loss_multiplier=z_loss_multiplier)
+
+    inputs = torch.randn(B, D, device=device, dtype=torch.bfloat16)
+    weight = torch.randn(V, D, device=device, dtype=torch.bfloat16)
+    target = torch.randint(0, V, (B,), device=device)
+    result = compiled_fn(inputs, weight, target)
+    expected = reference_linear_cross_entropy(inputs, weight.T, target, z_loss_multiplier=z_loss_multiplier)
+    assert torch.allclose(result.float(), expected.float(), rtol=5e-3, atol=5e-3)
+
+
+# --------------------------------------------------------------------------- oracle / golden parity
+
+def _dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.to(get_default_device())
+
+
+def _maxabs_norm(a, ref):
+    a = np.asarray(a, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return np.abs(a - ref).max() / max(np.abs(ref).max(), 1e-30)
+
+
+def _run(H, W, t, red, z, accum="fp32", requires=True):
+    Hd = _dev(H, torch.bfloat16).requires_grad_(requires)
+    Wd = _dev(W, torch.bfloat16).requires_grad_(requires)
+    loss = chunked_linear_cross_entropy(Hd, Wd, _dev(t), reduction=red, z_loss_multiplier=z, grad_weight_accum_dtype=accum)
+    if requires:
+        loss.backward()
+        return loss.item(), Hd.grad.float().cpu().numpy(), Wd.grad.float().cpu().numpy()
+    return loss.item(), None, None
+
+
+@requires_gpu
+@pytest.mark.parametrize("name,N,D,V,seed,wstd,ign", [("lce32x128x1000", 32, 128, 1000, 31, 1.0, 0.25), ("lce37x64x257c11", 37, 64, 257, 32, 1.0, 0.2)])
+@pytest.mark.parametrize("red", ["mean", "sum"])
+@pytest.mark.parametrize("z", [0.0, 1e-4])
+def test_lce_matches_golden(golden, name, N, D, V, seed, wstd, ign, red, z):
+    H, W, t = O.make_lce_inputs(N, D, V, seed, wstd, ign)
+    loss, gH, gW = _run(H, W, t, red, z)
+    key = f"{name}/{red}/z{z}"
+    ref = float(golden[f"{key}/loss"])
+    assert abs(loss - ref) <= 1e-3 * max(1.0, abs(ref))
+    assert _maxabs_norm(gH, golden[f"{key}/grad_H"]) <= 2e-2
+    assert _maxabs_norm(gW, golden[f"{key}/grad_W"]) <= 2e-2
+    lfo, _, _ = _run(H, W, t, red, z, requires=False)
+    assert abs(lfo - float(golden[f"{key}/loss_fwd_only"])) <= 1e-3 * max(1.0, abs(ref))
+
+
+@requires_gpu
+@pytest.mark.parametrize("z", [0.0, 1e-4])
+def test_lce_cfg1_matches_golden_and_oracle(golden, z):
+    """Workload cfg1 at full size (512 x 1024 x 32000)."""
+    H, W, t = O.make_lce_inputs(512, 1024, 32000, 0, 0.02, 0.05)
+    loss, gH, gW = _run(H, W, t, "mean", z)
+    key = f"cfg1/mean/z{z}"
+    ref = float(golden[f"{key}/loss"])
+    assert abs(loss - ref) <= 1e-3 * abs(ref)
+    hv = gH.reshape(-1)[golden[f"{key}/grad_H_sel"]]
+    wv = gW.reshape(-1)[golden[f"{key}/grad_W_sel"]]
+    assert _maxabs_norm(hv, golden[f"{key}/grad_H_vals"]) <= 2e-2
+    assert _maxabs_norm(wv, golden[f"{key}/grad_W_vals"]) <= 2e-2
+    oloss, odH, odW = O.chunked_linear_cross_entropy(H, W, t, -100, "mean", z)
+    assert abs(loss - oloss) <= 1e-3 * abs(oloss)
+    assert _maxabs_norm(gH, odH) <= 2e-2
+    assert _maxabs_norm(gW, odW) <= 2e-2
+    # ignore_index masking is exact: ignored rows have zero input gradient
+    assert np.all(gH[t == -100] == 0)
+
+
+@requires_gpu
+def test_lce_weight_accum_dtype_and_multi_chunk():
+    """Several chunks (chunk heuristic below N) and both accumulation dtypes."""
+    H, W, t = O.make_lce_inputs(1200, 256, 9000, 5, 0.05, 0.1)
+    for accum in ("fp32", "weight"):
+        loss, gH, gW = _run(H, W, t, "mean", 1e-4, accum)
+        oloss, odH, odW = O.chunked_linear_cross_entropy(H, W, t, -100, "mean", 1e-4, fp32_grad_weight_accum=accum == "fp32", chunk=256)
+        assert abs(loss - oloss) <= 1e-3 * abs(oloss)
+        assert _maxabs_norm(gH, odH) <= 2e-2
+        assert _maxabs_norm(gW, odW) <= (2e-2 if accum == "fp32" else 8e-2)
+
+
+@requires_gpu
+def test_lce_no_grad_inputs_take_forward_only_path():
+    H, W, t = O.make_lce_inputs(64, 128, 3000, 9, 0.1, 0.1)
+    l1, _, _ = _run(H, W, t, "mean", 0.0, requires=False)
+    l2, _, _ = _run(H, W, t, "mean", 0.0, requires=True)
+    assert abs(l1 - l2) <= 1e-3 * abs(l2)
