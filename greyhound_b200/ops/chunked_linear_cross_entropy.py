@@ -32,6 +32,7 @@ __all__ = [
     "ChunkedLinearCrossEntropyFunction",
     "chunked_linear_cross_entropy_fwd",
     "chunked_linear_cross_entropy_fwd_mean",
+    "chunked_linear_cross_entropy_loss",
 ]
 
 
@@ -107,6 +108,29 @@ def _(
     return _fake(inputs, weight)
 
 
+@torch.library.custom_op("greyhound::chunked_linear_cross_entropy_loss", mutates_args=())
+def chunked_linear_cross_entropy_loss(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    ignore_index: int = -100,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """Forward-only sums (ce_sum, z_sum, n_valid); no gradient buffers."""
+    return linear_cross_entropy_loss(inputs, weight, target, z_loss_multiplier, ignore_index)
+
+
+@chunked_linear_cross_entropy_loss.register_fake
+def _(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    ignore_index: int = -100,
+) -> tuple[Tensor, Tensor, Tensor]:
+    return _fake(inputs, weight)[:3]
+
+
 def _forward_only_chunked_ce(
     inputs: Tensor,
     weight: Tensor,
@@ -116,7 +140,7 @@ def _forward_only_chunked_ce(
     z_loss_multiplier: float,
 ) -> Tensor:
     """Forward-only path (no gradient buffers), ops/chunked_linear_cross_entropy.py:91-132."""
-    ce_sum, z_sum, n_valid = linear_cross_entropy_loss(
+    ce_sum, z_sum, n_valid = chunked_linear_cross_entropy_loss(
         inputs, weight, target, z_loss_multiplier, ignore_index
     )
     loss = ce_sum + z_loss_multiplier * z_sum

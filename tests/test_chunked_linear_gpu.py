@@ -20,6 +20,7 @@ from greyhound_b200.nn.functional import (
 from greyhound_b200.ops.chunked_linear_cross_entropy import (
     chunked_linear_cross_entropy_fwd,
     chunked_linear_cross_entropy_fwd_mean,
+    chunked_linear_cross_entropy_loss,
 )
 from greyhound_b200.testing import requires_gpu
 from greyhound_b200.utils import get_default_device
@@ -142,6 +143,7 @@ def test_chunked_linear_cross_entropy_fwd_opcheck(dtype):
         opcheck(chunked_linear_cross_entropy_fwd, (inputs, weight, target, 1e-4, True, -100), raise_exception=True)
         opcheck(chunked_linear_cross_entropy_fwd, (inputs, weight, target, 0.0, False, -100), raise_exception=True)
         opcheck(chunked_linear_cross_entropy_fwd_mean, (inputs, weight, target, 1e-4, True, -100), raise_exception=True)
+        opcheck(chunked_linear_cross_entropy_loss, (inputs, weight, target, 1e-4, -100), raise_exception=True)
 
 
 @requires_gpu
