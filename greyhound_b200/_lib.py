@@ -51,7 +51,19 @@ SIGNATURES: dict[str, tuple] = {
     "gh_sls_fwd": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _vp, _i32, _vp, _vp, _sz, _vp]),
     "gh_sls_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i64, _i64, _i32, _vp, _vp]),
     "gh_logits_grad": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i64, _i64, _vp, _vp]),
+    "gh_lce_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i32, _i32]),
+    "gh_lce_fwd_bwd": (
+        _i32,
+        [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _i64, _i32, _i32,
+         _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    ),
+    "gh_lce_dh_last_chunk": (_i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _vp, _vp, _sz, _i32, _vp]),
+    "gh_gemm": (
+        _i32,
+        [_vp, _i64, _i32, _vp, _i64, _i32, _i64, _i64, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _vp, _vp, _vp],
+    ),
 }
+GH_LCE_DEFER_LAST_DH = 1
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -1,0 +1,427 @@
+// Chunked linear cross-entropy on the tcgen05 GEMM, plus the generic GEMM
+// entry point used by the bring-your-own-loss path.
+//
+// Per row chunk [s, e) (the reference loop, src/greyhound/ops/chunked_linear_loss.py:79-101,
+// with the CE callback of src/greyhound/ops/chunked_linear_cross_entropy.py:43-59):
+//   1. logits GEMM with the fused CE epilogue: bf16 logits tile to the
+//      workspace + per-(row, 256-column tile) (max, sum-exp) + target logit
+//   2. row combine: exact logsumexp per row, per-row ce / z terms
+//   3. logits -> dlogits in place: softmax * (1 + 2 z lse) * s - s * onehot
+//      (s = 1/max(n_valid,1) for the mean, folded in here instead of two
+//      mul_ passes over grad_input / grad_weight afterwards)
+//   4. dW GEMM (H^T @ dlogits), written as [D, V]; fp32 or weight-dtype
+//      accumulation across chunks through the epilogue addend
+//   5. dH GEMM (dlogits @ W), rows [s, e) of grad_input
+// and once at the end a fixed-order reduction of the per-row loss terms.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "row_ops.cuh"
+#include "tc_gemm.cuh"
+
+namespace gh {
+namespace {
+
+using gemm::BK;
+using gemm::BM;
+using gemm::BN;
+
+// ---------------------------------------------------------------------------
+// Tensor maps
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D map over a row-major matrix [outer, inner] with row pitch `ld`
+// elements, box {64, box_outer}, 128-byte swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t inner, int64_t outer, int64_t ld,
+             int box_outer) {
+  auto enc = get_encode();
+  if (!enc) return set_error(GH_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  const int elt = elt_size(dtype);
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * elt) & 15))
+    return set_error(GH_EUNSUPPORTED, "GEMM operand needs a 16-byte aligned base and row pitch (pitch %lld elements)",
+                     (long long)ld);
+  CUtensorMapDataType dt = dtype == GH_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t gstride[1] = {(cuuint64_t)(ld * elt)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(ptr), gdim, gstride, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(GH_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GH_OK;
+}
+
+int num_sms_dev() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int cached[64] = {0};
+  if (dev < 64 && cached[dev]) return cached[dev];
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev < 64) cached[dev] = n;
+  return n;
+}
+
+// One GEMM operand: pointer, pitch, majorness.
+struct Operand {
+  const void* ptr;
+  int64_t ld;
+  int mn_major;  // 0: [rows, K] K contiguous; 1: [K, rows] rows contiguous
+};
+
+template <typename T, int A_MN, int B_MN, int EPI, typename OutT>
+int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p, int max_ctas, cudaStream_t st) {
+  auto kern = gemm::tc_gemm_kernel<T, A_MN, B_MN, EPI, OutT>;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES);
+    if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_done[dev] = true;
+  }
+  int grid = p.num_tiles < max_ctas ? p.num_tiles : max_ctas;
+  if (grid <= 0) return GH_OK;
+  kern<<<grid, gemm::THREADS, gemm::SMEM_BYTES, st>>>(ta, tb, p);
+  count_launch(1);
+  return check_launch("tc_gemm");
+}
+
+// Dispatch on majorness for a fixed (T, EPI, OutT).
+template <typename T, int EPI, typename OutT>
+int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b_mn, gemm::Params& p,
+                   int max_ctas, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT>(ta, tb, p, max_ctas, st);
+  if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT>(ta, tb, p, max_ctas, st);
+  if (a_mn && !b_mn) return launch_gemm_t<T, 1, 0, EPI, OutT>(ta, tb, p, max_ctas, st);
+  return launch_gemm_t<T, 1, 1, EPI, OutT>(ta, tb, p, max_ctas, st);
+}
+
+// Generic: D[M,N] = scale * A B^T (+ addend), D written as out_dtype with pitch ldo.
+int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N, int64_t K, void* out,
+             int out_dtype, int64_t ldo, const float* add_f32, const void* add_same, int64_t ldadd,
+             const float* scale, int raster, int max_ctas, cudaStream_t st, int* status) {
+  if (M <= 0 || N <= 0) return GH_OK;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return set_error(GH_EINVAL, "GEMM dimension too large");
+  CUtensorMap ta, tb;
+  int rc;
+  if (A.mn_major) rc = make_map(&ta, A.ptr, dtype, M, K, A.ld, BK);
+  else rc = make_map(&ta, A.ptr, dtype, K, M, A.ld, BM);
+  if (rc) return rc;
+  if (B.mn_major) rc = make_map(&tb, B.ptr, dtype, N, K, B.ld, BK);
+  else rc = make_map(&tb, B.ptr, dtype, K, N, B.ld, BN);
+  if (rc) return rc;
+  gemm::Params p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + BN - 1) / BN);
+  p.num_tiles = p.num_m * p.num_n;
+  p.raster = raster;
+  p.out = out;
+  p.ldo = ldo;
+  const int oelt = elt_size(out_dtype);
+  p.vec_ok = ((reinterpret_cast<uintptr_t>(out) | (uintptr_t)(ldo * oelt)) & 15) == 0;
+  if (add_f32) p.vec_ok &= ((reinterpret_cast<uintptr_t>(add_f32) | (uintptr_t)(ldadd * 4)) & 15) == 0;
+  if (add_same) p.vec_ok &= ((reinterpret_cast<uintptr_t>(add_same) | (uintptr_t)(ldadd * oelt)) & 15) == 0;
+  p.add_f32 = add_f32;
+  p.add_same = add_same;
+  p.ldadd = ldadd;
+  p.scale = scale;
+  p.status = status;
+  if (max_ctas <= 0) max_ctas = num_sms_dev();
+  if (dtype == GH_BF16) {
+    if (out_dtype == GH_F32) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
+    if (out_dtype == GH_BF16) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
+  } else if (dtype == GH_F16) {
+    if (out_dtype == GH_F32) return launch_gemm_mm<__half, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
+    if (out_dtype == GH_F16) return launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
+  }
+  return set_error(GH_ETYPE, "unsupported GEMM dtype combination (%d -> %d)", dtype, out_dtype);
+}
+
+// ---------------------------------------------------------------------------
+// Linear-CE helper kernels
+
+// Exact per-row logsumexp from the epilogue's per-tile (max, sum) pairs and
+// the per-row loss terms (kernels/cross_entropy.py:84-92).
+__global__ void __launch_bounds__(256)
+lce_combine_kernel(const float2* __restrict__ stats, int num_n, int64_t rows, const float* __restrict__ xt,
+                   const int64_t* __restrict__ labels, int64_t V, int64_t ignore, float* lse_out, float* row_ce,
+                   float* row_z, int* status) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  MS acc = ms_empty();
+  for (int j = 0; j < num_n; ++j) {
+    const float2 p = stats[(int64_t)j * rows + r];
+    acc = ms_merge(acc, MS{p.x, p.y});
+  }
+  const float lse = (acc.m + fast_log2(acc.s)) * kLn2;
+  const int64_t lab = labels[r];
+  bool valid = lab != ignore;
+  if (valid && (lab < 0 || lab >= V)) {
+    atomicOr(status, GH_DEV_BAD_LABEL);
+    valid = false;
+  }
+  lse_out[r] = lse;
+  row_ce[r] = valid ? lse - xt[r] : 0.f;
+  row_z[r] = valid ? lse * lse : 0.f;
+}
+
+// In-place logits -> dlogits over a pitched [rows, ld] buffer; grid (rows, chunks).
+template <typename T, int THREADS>
+__global__ void __launch_bounds__(THREADS)
+lce_dlogits_kernel(T* logits, int64_t ld, const int64_t* __restrict__ labels, const float* __restrict__ lse,
+                   int64_t V, int64_t chunk, float zmul, int64_t ignore, const float* scale_ptr) {
+  const int64_t row = blockIdx.x;
+  const int64_t c0 = (int64_t)blockIdx.y * chunk;
+  if (c0 >= V) return;
+  const int64_t n = c0 + chunk < V ? chunk : V - c0;
+  const int64_t lab = labels[row];
+  T* y = logits + row * ld + c0;
+  if (lab == ignore || lab < 0 || lab >= V) {
+    row_zero<T, THREADS>(y, n);
+    return;
+  }
+  const float l = lse[row];
+  const float scale = scale_ptr ? *scale_ptr : 1.f;
+  const float coef = scale * (1.f + 2.f * zmul * l);
+  row_grad<T, THREADS, kUnroll>(y, y, n, lab - c0, l * kLog2e, coef, scale);
+}
+
+struct LceLayout {
+  size_t status = 0, scale = 64;
+  size_t logits, stats, xt, lse, row_ce, row_z, acc, total;
+  int64_t chunk, ldl;
+  int num_n;
+  bool need_acc;
+};
+
+inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
+LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, int fp32_accum) {
+  LceLayout L;
+  if (chunk <= 0 || chunk > N) chunk = N;
+  L.chunk = chunk;
+  L.ldl = (V + 7) / 8 * 8;  // 16-byte row pitch for TMA
+  L.num_n = (int)((V + BN - 1) / BN);
+  const int elt = elt_size(dtype);
+  size_t off = 256;
+  L.logits = off; off = al256(off + (size_t)chunk * L.ldl * elt);
+  L.stats = off;  off = al256(off + sizeof(float2) * (size_t)L.num_n * chunk);
+  L.xt = off;     off = al256(off + sizeof(float) * chunk);
+  L.lse = off;    off = al256(off + sizeof(float) * chunk);
+  L.row_ce = off; off = al256(off + sizeof(float) * N);
+  L.row_z = off;  off = al256(off + sizeof(float) * N);
+  const int64_t nchunks = N > 0 ? (N + chunk - 1) / chunk : 0;
+  L.need_acc = fp32_accum && nchunks > 1;
+  L.acc = off;
+  if (L.need_acc) off = al256(off + sizeof(float) * (size_t)D * V);
+  L.total = off;
+  return L;
+}
+
+template <typename T>
+int lce_dlogits(T* logits, int64_t ld, const int64_t* labels, const float* lse, int64_t rows, int64_t V,
+                float zmul, int64_t ignore, const float* scale, cudaStream_t st) {
+  if (rows <= 0) return GH_OK;
+  const int sms = num_sms_dev();
+  int64_t want = (8 * (int64_t)sms + rows - 1) / rows;
+  int64_t max_by_size = (V + 4095) / 4096;
+  int64_t s = want < max_by_size ? want : max_by_size;
+  if (s < 1) s = 1;
+  const int per = 16 / (int)sizeof(T);
+  int64_t chunk = (V + s - 1) / s;
+  chunk = (chunk + per - 1) / per * per;
+  s = (V + chunk - 1) / chunk;
+  dim3 grid((unsigned)rows, (unsigned)s);
+  lce_dlogits_kernel<T, 256><<<grid, 256, 0, st>>>(logits, ld, labels, lse, V, chunk, zmul, ignore, scale);
+  count_launch(1);
+  return check_launch("lce_dlogits");
+}
+
+template <typename T>
+int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int64_t D, int64_t V, int dtype,
+            float zmul, int64_t ignore, int mean, const float* grad_scale, const LceLayout& L, int flags,
+            void* grad_input, void* grad_weight, float* ce_sum, float* z_sum, float* n_valid, char* ws,
+            cudaStream_t st) {
+  int* status = reinterpret_cast<int*>(ws + L.status);
+  float* scale = reinterpret_cast<float*>(ws + L.scale);
+  T* logits = reinterpret_cast<T*>(ws + L.logits);
+  float2* stats = reinterpret_cast<float2*>(ws + L.stats);
+  float* xt = reinterpret_cast<float*>(ws + L.xt);
+  float* lse = reinterpret_cast<float*>(ws + L.lse);
+  float* row_ce = reinterpret_cast<float*>(ws + L.row_ce);
+  float* row_z = reinterpret_cast<float*>(ws + L.row_z);
+  float* acc = reinterpret_cast<float*>(ws + L.acc);
+  const bool with_grad = grad_input || grad_weight;
+  const bool fp32_accum = L.need_acc;
+  int rc = GH_OK;
+  cudaMemsetAsync(status, 0, sizeof(int), st);
+  const float* sp = grad_scale;
+  if (with_grad && mean) {
+    mean_scale_kernel<<<1, 1024, 0, st>>>(target, N, ignore, grad_scale, scale);
+    count_launch(1);
+    sp = scale;
+  }
+  const int64_t nchunks = (N + L.chunk - 1) / L.chunk;
+  const int sms = num_sms_dev();
+  for (int64_t c = 0; c < nchunks; ++c) {
+    const int64_t s0 = c * L.chunk;
+    const int64_t rows = (s0 + L.chunk <= N) ? L.chunk : N - s0;
+    const T* Hc = static_cast<const T*>(H) + s0 * D;
+    const int64_t* tc = target + s0;
+    // 1. logits GEMM + fused CE statistics
+    {
+      CUtensorMap ta, tb;
+      if ((rc = make_map(&ta, Hc, dtype, D, rows, D, BM))) return rc;
+      if ((rc = make_map(&tb, W, dtype, D, V, D, BN))) return rc;
+      gemm::Params p{};
+      p.M = (int)rows;
+      p.N = (int)V;
+      p.K = (int)D;
+      p.num_m = (int)((rows + BM - 1) / BM);
+      p.num_n = L.num_n;
+      p.num_tiles = p.num_m * p.num_n;
+      p.raster = 0;  // m fastest: concurrent CTAs share one W band, H stays in L2
+      p.out = logits;
+      p.ldo = L.ldl;
+      p.vec_ok = ((L.ldl * (int64_t)sizeof(T)) & 15) == 0;
+      p.labels = tc;
+      p.stats = stats;
+      p.xt = xt;
+      p.status = status;
+      if ((rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T>(ta, tb, p, sms, st))) return rc;
+    }
+    // 2. per-row logsumexp and loss terms
+    lce_combine_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(stats, L.num_n, rows, xt, tc, V, ignore, lse,
+                                                                      row_ce + s0, row_z + s0, status);
+    count_launch(1);
+    if ((rc = check_launch("lce_combine"))) return rc;
+    if (!with_grad) continue;
+    // 3. dlogits in place
+    if ((rc = lce_dlogits<T>(logits, L.ldl, tc, lse, rows, V, zmul, ignore, sp, st))) return rc;
+    // 4. dW[D, V] (+)= H_c^T @ dlogits_c
+    if (grad_weight) {
+      const bool first = c == 0, last = c == nchunks - 1;
+      Operand A{Hc, D, 1};
+      Operand B{logits, L.ldl, 1};
+      void* out;
+      int out_dtype;
+      const float* add_f32 = nullptr;
+      const void* add_same = nullptr;
+      if (fp32_accum) {
+        out = last ? grad_weight : (void*)acc;
+        out_dtype = last ? dtype : GH_F32;
+        add_f32 = first ? nullptr : acc;
+      } else {
+        out = grad_weight;
+        out_dtype = dtype;
+        add_same = first ? nullptr : grad_weight;
+      }
+      if ((rc = run_gemm(dtype, A, B, D, V, rows, out, out_dtype, V, add_f32, add_same, V, nullptr, 0, sms, st,
+                         status)))
+        return rc;
+    }
+    // 5. dH rows [s0, s0 + rows) = dlogits_c @ W
+    if (grad_input && !((flags & GH_LCE_DEFER_LAST_DH) && c == nchunks - 1)) {
+      Operand A{logits, L.ldl, 0};
+      Operand B{W, D, 1};
+      if ((rc = run_gemm(dtype, A, B, rows, D, V, static_cast<T*>(grad_input) + s0 * D, dtype, D, nullptr, nullptr,
+                         0, nullptr, 1, sms, st, status)))
+        return rc;
+    }
+  }
+  ce_finalize_kernel<<<1, 1024, 0, st>>>(row_ce, row_z, target, N, ignore, ce_sum, z_sum, n_valid);
+  count_launch(1);
+  return check_launch("lce_finalize");
+}
+
+}  // namespace
+}  // namespace gh
+
+using namespace gh;
+
+extern "C" size_t gh_lce_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows, int dtype,
+                                         int fp32_grad_weight_accum) {
+  if (N < 0 || D <= 0 || V <= 0 || elt_size(dtype) != 2) return 0;
+  return lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum).total;
+}
+
+extern "C" int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target, int64_t N, int64_t D, int64_t V,
+                              int dtype, float z_loss_multiplier, int64_t ignore_index, int mean_reduction,
+                              const float* grad_scale, int64_t chunk_rows, int fp32_grad_weight_accum, int flags,
+                              void* grad_input, void* grad_weight, float* ce_sum, float* z_sum, float* n_valid,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16)
+    return set_error(GH_ETYPE, "linear cross-entropy kernels take bf16 or fp16 operands (dtype code %d)", dtype);
+  if (N < 0 || D <= 0 || V <= 0) return set_error(GH_EINVAL, "bad shape N=%lld D=%lld V=%lld", (long long)N,
+                                                   (long long)D, (long long)V);
+  if (D % 8) return set_error(GH_EUNSUPPORTED, "hidden size must be a multiple of 8 (got %lld)", (long long)D);
+  if (!H || !W || !target || !ce_sum || !z_sum || !n_valid || !workspace)
+    return set_error(GH_EINVAL, "null pointer argument");
+  LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum);
+  if (workspace_bytes < L.total)
+    return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  if (N == 0) {
+    ce_finalize_kernel<<<1, 1024, 0, st>>>(nullptr, nullptr, target, 0, ignore_index, ce_sum, z_sum, n_valid);
+    count_launch(1);
+    return check_launch("lce_finalize");
+  }
+  if (dtype == GH_BF16)
+    return lce_run<__nv_bfloat16>(H, W, target, N, D, V, dtype, z_loss_multiplier, ignore_index, mean_reduction,
+                                  grad_scale, L, flags, grad_input, grad_weight, ce_sum, z_sum, n_valid, ws, st);
+  return lce_run<__half>(H, W, target, N, D, V, dtype, z_loss_multiplier, ignore_index, mean_reduction, grad_scale,
+                         L, flags, grad_input, grad_weight, ce_sum, z_sum, n_valid, ws, st);
+}
+
+extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype, int64_t chunk_rows,
+                                    int fp32_grad_weight_accum, void* grad_input, void* workspace,
+                                    size_t workspace_bytes, int max_ctas, void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
+  if (N <= 0) return GH_OK;
+  LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum);
+  if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small");
+  char* ws = static_cast<char*>(workspace);
+  const int64_t nchunks = (N + L.chunk - 1) / L.chunk;
+  const int64_t s0 = (nchunks - 1) * L.chunk;
+  const int64_t rows = N - s0;
+  Operand A{ws + L.logits, L.ldl, 0};
+  Operand B{W, D, 1};
+  const int elt = elt_size(dtype);
+  return run_gemm(dtype, A, B, rows, D, V, static_cast<char*>(grad_input) + s0 * D * elt, dtype, D, nullptr, nullptr,
+                  0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status));
+}
+
+extern "C" int gh_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
+                       int64_t M, int64_t N, int64_t K, int dtype, void* out, int64_t ldo, int out_dtype,
+                       const void* addend, int64_t ld_add, const float* scale, int* status, void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "GEMM operands must be bf16 or fp16");
+  if (M < 0 || N < 0 || K <= 0) return set_error(GH_EINVAL, "bad GEMM shape");
+  Operand a{A, lda, a_mn_major ? 1 : 0};
+  Operand b{B, ldb, b_mn_major ? 1 : 0};
+  const float* add_f32 = out_dtype == GH_F32 ? static_cast<const float*>(addend) : nullptr;
+  const void* add_same = out_dtype == GH_F32 ? nullptr : addend;
+  const int raster = M >= N ? 1 : 0;
+  return run_gemm(dtype, a, b, M, N, K, out, out_dtype, ldo, add_f32, add_same, ld_add, scale, raster, 0,
+                  static_cast<cudaStream_t>(stream), status);
+}

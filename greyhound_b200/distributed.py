@@ -65,8 +65,8 @@ class RowShardedLinearCrossEntropy(torch.autograd.Function):
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         hook = None
         if world > 1:
-            def hook(grad_weight: Tensor) -> None:
-                dist.all_reduce(grad_weight, group=group)
+            def hook(grad_weight: Tensor):
+                return dist.all_reduce(grad_weight, group=group, async_op=True)
         ce, zs, _, gi, gw = lce.linear_cross_entropy_with_grad(
             inputs, weight_dv, target, z_loss_multiplier, fp32_accum, ignore_index,
             grad_scale=scale, grad_weight_hook=hook,

@@ -54,6 +54,70 @@ def _check(inputs: Tensor, weight: Tensor, target: Tensor) -> None:
         raise ValueError("expected inputs, weight and target on the same CUDA device")
 
 
+def _tc_ok(inputs: Tensor, weight: Tensor) -> bool:
+    """bf16/fp16 with a hidden size that gives 16-byte rows -> tcgen05 pipeline.
+    fp32 (the reference's opcheck dtype) stays on cuBLAS GEMMs + the row kernel."""
+    return (
+        inputs.dtype in (torch.bfloat16, torch.float16)
+        and weight.dtype == inputs.dtype
+        and inputs.shape[1] % 8 == 0
+    )
+
+
+def _weight_vd(weight: Tensor) -> Tensor:
+    """The [V, D] row-major matrix behind the [D, V] operand (a view when it is W.T)."""
+    w = weight.T
+    return w if w.is_contiguous() else w.contiguous()
+
+
+def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scale, with_grad,
+            grad_weight_hook=None):
+    from greyhound_b200 import _lib
+
+    B, D = inputs.shape
+    V = weight.shape[1]
+    x = inputs.contiguous()
+    w = _weight_vd(weight)
+    t = target.contiguous()
+    dev = inputs.device
+    chunk = chunk_size_for(B, D, V, inputs.element_size())
+    lib = _lib.load()
+    code = _lib.dtype_code(inputs.dtype)
+    ws = _lib.workspace(lib.gh_lce_workspace_bytes(B, D, V, chunk, code, int(fp32_accum)), dev)
+    ce_sum = torch.empty((), dtype=torch.float32, device=dev)
+    z_sum = torch.empty((), dtype=torch.float32, device=dev)
+    n_valid = torch.empty((), dtype=torch.float32, device=dev)
+    gi = torch.empty((B, D), dtype=inputs.dtype, device=dev) if with_grad else None
+    gw = torch.empty((D, V), dtype=weight.dtype, device=dev) if with_grad else None
+    gs = grad_scale.reshape(1).float().contiguous() if grad_scale is not None else None
+    defer = with_grad and grad_weight_hook is not None and B > 0
+    stream = _lib.stream_of(inputs)
+    st = lib.gh_lce_fwd_bwd(
+        x.data_ptr(), w.data_ptr(), t.data_ptr(), B, D, V, code, float(z), int(ignore_index),
+        int(mean), _lib.ptr(gs), chunk, int(fp32_accum),
+        _lib.GH_LCE_DEFER_LAST_DH if defer else 0,
+        _lib.ptr(gi), _lib.ptr(gw), ce_sum.data_ptr(), z_sum.data_ptr(), n_valid.data_ptr(),
+        ws.data_ptr(), ws.numel(), stream,
+    )
+    _lib.check(st, "linear_cross_entropy")
+    if defer:
+        work = grad_weight_hook(gw)
+        # leave SMs free for the collective while the deferred dH GEMM runs
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        st = lib.gh_lce_dh_last_chunk(
+            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), gi.data_ptr(), ws.data_ptr(), ws.numel(),
+            max(1, sms - 20), stream,
+        )
+        _lib.check(st, "linear_cross_entropy dH")
+        if work is not None:
+            work.wait()
+    elif with_grad and grad_weight_hook is not None:
+        w_ = grad_weight_hook(gw)
+        if w_ is not None:
+            w_.wait()
+    return ce_sum, z_sum, n_valid, gi, gw
+
+
 def linear_cross_entropy_with_grad(
     inputs: Tensor,
     weight: Tensor,
@@ -73,6 +137,10 @@ def linear_cross_entropy_with_grad(
     the final weight gradient exists (the data-parallel all-reduce hooks in here).
     """
     _check(inputs, weight, target)
+    if _tc_ok(inputs, weight):
+        return _tc_lce(inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index,
+                       mean_reduction, grad_scale, True, grad_weight_hook)
+    # fp32 operands: cuBLAS GEMMs around the CE row kernel
     B, D = inputs.shape
     V = weight.shape[1]
     chunk = chunk_size_for(B, D, V, inputs.element_size())
@@ -102,7 +170,9 @@ def linear_cross_entropy_with_grad(
         torch.addmm(grad_weight_acc, x.T, logits, out=grad_weight_acc, out_dtype=acc_dtype)
     grad_weight = grad_weight_acc.to(weight.dtype)
     if grad_weight_hook is not None:
-        grad_weight_hook(grad_weight)
+        work = grad_weight_hook(grad_weight)
+        if work is not None:
+            work.wait()
     return ce_sum, z_sum, n_valid, grad_input, grad_weight
 
 
@@ -115,6 +185,10 @@ def linear_cross_entropy_loss(
 ) -> tuple[Tensor, Tensor, Tensor]:
     """Forward only: ``(ce_sum, z_sum, n_valid)``, no gradient buffers."""
     _check(inputs, weight, target)
+    if _tc_ok(inputs, weight):
+        ce, z, n, _, _ = _tc_lce(inputs, weight, target, z_loss_multiplier, True, ignore_index,
+                                 False, None, False)
+        return ce, z, n
     B, D = inputs.shape
     V = weight.shape[1]
     chunk = chunk_size_for(B, D, V, inputs.element_size())

@@ -132,6 +132,66 @@ GH_API int gh_logits_grad(const void* logits, void* dlogits, const int64_t* labe
                           float z_loss_multiplier, int64_t ignore_index,
                           int64_t label_offset, const float* grad_scale, void* stream);
 
+/* ------------------------------------------------------------------------ *
+ * Chunked linear cross-entropy, forward + backward, on tcgen05 GEMMs.
+ * Replaces the op greyhound::chunked_linear_cross_entropy_fwd
+ * (src/greyhound/ops/chunked_linear_cross_entropy.py:19-67) and the chunk
+ * loop it drives (src/greyhound/ops/chunked_linear_loss.py:56-103).
+ *
+ *   H      [N, D] activations, dtype BF16 or F16 (row-major)
+ *   W      [V, D] weight, same dtype (row-major; the reference passes the
+ *          [D, V] view W.T, which is this same memory)
+ *   target [N] int64 class ids or ignore_index
+ *   chunk_rows: rows per chunk (<= 0: all rows in one chunk); the logits of
+ *          one chunk ([chunk, V] in the activation dtype) live in the workspace
+ *   grad_input  [N, D] (same dtype) or NULL
+ *   grad_weight [D, V] (same dtype, the layout of the reference op's output)
+ *          or NULL; both NULL -> loss only
+ *   fp32_grad_weight_accum: 1 -> weight gradient accumulated across chunks in
+ *          fp32 and cast once; 0 -> accumulated in the weight dtype
+ *   mean_reduction / grad_scale: as for gh_ce_fwd_grad; the scale is folded
+ *          into the logits gradient, so both gradients come out scaled
+ *   flags: GH_LCE_DEFER_LAST_DH -> the last chunk's grad_input rows are not
+ *          computed; call gh_lce_dh_last_chunk later (lets a data-parallel
+ *          caller start the grad_weight all-reduce first)
+ *   ce_sum, z_sum, n_valid: float scalars (overwritten)
+ * ------------------------------------------------------------------------ */
+enum { GH_LCE_DEFER_LAST_DH = 1 };
+
+GH_API size_t gh_lce_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows,
+                                     int dtype, int fp32_grad_weight_accum);
+GH_API int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target,
+                          int64_t N, int64_t D, int64_t V, int dtype,
+                          float z_loss_multiplier, int64_t ignore_index,
+                          int mean_reduction, const float* grad_scale,
+                          int64_t chunk_rows, int fp32_grad_weight_accum, int flags,
+                          void* grad_input, void* grad_weight,
+                          float* ce_sum, float* z_sum, float* n_valid,
+                          void* workspace, size_t workspace_bytes, void* stream);
+/* grad_input rows of the last chunk, from the dlogits left in the workspace by
+ * gh_lce_fwd_bwd(..., GH_LCE_DEFER_LAST_DH). max_ctas <= 0: all SMs. */
+GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype,
+                                int64_t chunk_rows, int fp32_grad_weight_accum,
+                                void* grad_input, void* workspace, size_t workspace_bytes,
+                                int max_ctas, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Plain tcgen05 GEMM (the GEMMs of the generic chunked_linear_loss path,
+ * src/greyhound/ops/chunked_linear_loss.py:82,94,95-101):
+ *   out[M, N] = scale * sum_k A[m, k] B[n, k]  (+ addend[M, N])
+ * A is [M, K] with pitch lda (a_mn_major = 0) or [K, M] (a_mn_major = 1);
+ * B likewise [N, K] / [K, N]. Operands BF16 or F16, 16-byte aligned with
+ * 16-byte row pitches. out_dtype F32 or the operand dtype; the addend has
+ * the output dtype and pitch ld_add (may alias out for accumulation).
+ * status: optional device int receiving error bits.
+ * ------------------------------------------------------------------------ */
+GH_API int gh_gemm(const void* A, int64_t lda, int a_mn_major,
+                   const void* B, int64_t ldb, int b_mn_major,
+                   int64_t M, int64_t N, int64_t K, int dtype,
+                   void* out, int64_t ldo, int out_dtype,
+                   const void* addend, int64_t ld_add, const float* scale,
+                   int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

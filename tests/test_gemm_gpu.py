@@ -1,0 +1,53 @@
+"""tcgen05 GEMM (gh_gemm) against a torch fp32 matmul of the same bf16/fp16 values,
+for all four operand-majorness combinations, odd shapes and both epilogue
+addend/scale forms."""
+
+import pytest
+import torch
+
+from greyhound_b200.kernels.gemm import gemm_nt
+from greyhound_b200.testing import requires_gpu
+
+
+def _view(x: torch.Tensor, mn_major: bool) -> torch.Tensor:
+    # [R, K] view that is either row-major or the transpose of a row-major [K, R]
+    return x.T.contiguous().T if mn_major else x.contiguous()
+
+
+def _rel(a, b):
+    return ((a.double() - b.double()).norm() / b.double().norm().clamp(min=1e-30)).item()
+
+
+@requires_gpu
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (200, 296, 136), (1000, 1304, 1000), (2048, 4096, 4096)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_matches_torch(a_mn, b_mn, M, N, K, dtype):
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N * 3 + K)
+    a = torch.randn(M, K, device="cuda", generator=g).to(dtype)
+    b = torch.randn(N, K, device="cuda", generator=g).to(dtype)
+    ref = a.float() @ b.float().T
+    out32 = gemm_nt(_view(a, a_mn), _view(b, b_mn), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert _rel(out32, ref) < 1e-5 * K ** 0.5 + 1e-6
+    out16 = gemm_nt(_view(a, a_mn), _view(b, b_mn))
+    assert out16.dtype == dtype
+    assert _rel(out16.float(), ref) < 1e-2
+
+
+@requires_gpu
+def test_gemm_addend_and_scale():
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(384, 512, device="cuda", generator=g).to(torch.bfloat16)
+    b = torch.randn(640, 512, device="cuda", generator=g).to(torch.bfloat16)
+    acc = torch.randn(384, 640, device="cuda", generator=g)
+    scale = torch.tensor([0.25], device="cuda")
+    ref = acc + 0.25 * (a.float() @ b.float().T)
+    out = gemm_nt(a, b, out=acc, addend=acc, scale=scale)  # in-place accumulate
+    assert out.data_ptr() == acc.data_ptr()
+    assert _rel(out, ref) < 1e-5
+    accb = torch.randn(384, 640, device="cuda", generator=g).to(torch.bfloat16)
+    ref = accb.float() + a.float() @ b.float().T
+    out = gemm_nt(a, b, out=accb, addend=accb)
+    assert _rel(out.float(), ref) < 1e-2
