@@ -9,7 +9,7 @@
 //   3. logits -> dlogits in place: softmax * (1 + 2 z lse) * s - s * onehot
 //      (s = 1/max(n_valid,1) for the mean, folded in here instead of two
 //      mul_ passes over grad_input / grad_weight afterwards)
-//   4. dW GEMM (H^T @ dlogits), written as [D, V]; fp32 or weight-dtype
+//   4. dW GEMM (dlogits^T @ H), written as [V, D]; fp32 or weight-dtype
 //      accumulation across chunks through the epilogue addend
 //   5. dH GEMM (dlogits @ W), rows [s, e) of grad_input
 // and once at the end a fixed-order reduction of the per-row loss terms.
@@ -85,32 +85,97 @@ struct Operand {
   int mn_major;  // 0: [rows, K] K contiguous; 1: [K, rows] rows contiguous
 };
 
-template <typename T, int A_MN, int B_MN, int EPI, typename OutT>
+template <typename T, int A_MN, int B_MN, int EPI, typename OutT, int PAIR>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p, int max_ctas, cudaStream_t st) {
-  auto kern = gemm::tc_gemm_kernel<T, A_MN, B_MN, EPI, OutT>;
-  static bool attr_done[64] = {false};
+  auto kern = gemm::tc_gemm_kernel<T, A_MN, B_MN, EPI, OutT, PAIR>;
+  constexpr int SMEM = gemm::Geo<PAIR>::SMEM;
+  static int max_units[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm::SMEM_BYTES);
+  if (dev >= 64) return set_error(GH_EUNSUPPORTED, "device index >= 64");
+  if (!max_units[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-    attr_done[dev] = true;
+    int units = num_sms_dev() / PAIR;
+    if (PAIR > 1) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(units * PAIR);
+      cfg.blockDim = dim3(gemm::THREADS);
+      cfg.dynamicSmemBytes = SMEM;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = PAIR;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0 && n < units) units = n;
+      cudaGetLastError();
+    }
+    max_units[dev] = units;
   }
-  int grid = p.num_tiles < max_ctas ? p.num_tiles : max_ctas;
-  if (grid <= 0) return GH_OK;
-  kern<<<grid, gemm::THREADS, gemm::SMEM_BYTES, st>>>(ta, tb, p);
+  int units = max_units[dev];
+  if (max_ctas > 0 && max_ctas / PAIR < units) units = max_ctas / PAIR > 0 ? max_ctas / PAIR : 1;
+  if (p.num_tiles < units) units = p.num_tiles;
+  if (units <= 0) return GH_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(units * PAIR);
+  cfg.blockDim = dim3(gemm::THREADS);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = PAIR;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) return set_error(GH_ECUDA, "tc_gemm launch: %s", cudaGetErrorString(e));
   count_launch(1);
   return check_launch("tc_gemm");
 }
 
-// Dispatch on majorness for a fixed (T, EPI, OutT).
+// Dispatch on majorness and pairing for a fixed (T, EPI, OutT).
 template <typename T, int EPI, typename OutT>
-int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b_mn, gemm::Params& p,
+int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b_mn, int pair, gemm::Params& p,
                    int max_ctas, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT>(ta, tb, p, max_ctas, st);
-  if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT>(ta, tb, p, max_ctas, st);
-  if (a_mn && !b_mn) return launch_gemm_t<T, 1, 0, EPI, OutT>(ta, tb, p, max_ctas, st);
-  return launch_gemm_t<T, 1, 1, EPI, OutT>(ta, tb, p, max_ctas, st);
+  if (pair == 2) {
+    if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT, 2>(ta, tb, p, max_ctas, st);
+    if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT, 2>(ta, tb, p, max_ctas, st);
+    if (a_mn && !b_mn) return launch_gemm_t<T, 1, 0, EPI, OutT, 2>(ta, tb, p, max_ctas, st);
+    return launch_gemm_t<T, 1, 1, EPI, OutT, 2>(ta, tb, p, max_ctas, st);
+  }
+  if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT, 1>(ta, tb, p, max_ctas, st);
+  if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT, 1>(ta, tb, p, max_ctas, st);
+  if (a_mn && !b_mn) return launch_gemm_t<T, 1, 0, EPI, OutT, 1>(ta, tb, p, max_ctas, st);
+  return launch_gemm_t<T, 1, 1, EPI, OutT, 1>(ta, tb, p, max_ctas, st);
+}
+
+// 2-CTA tiles (256 rows) once there are more than 128 rows.
+inline int pick_pair(int64_t M) { return M > BM ? 2 : 1; }
+
+// Tensor maps of both operands for a GEMM of M x N x K with pairing `pair`.
+int make_operand_maps(CUtensorMap* ta, CUtensorMap* tb, int dtype, const Operand& A, const Operand& B, int64_t M,
+                      int64_t N, int64_t K, int pair) {
+  int rc;
+  if (A.mn_major) rc = make_map(ta, A.ptr, dtype, M, K, A.ld, BK);
+  else rc = make_map(ta, A.ptr, dtype, K, M, A.ld, BM);
+  if (rc) return rc;
+  if (B.mn_major) rc = make_map(tb, B.ptr, dtype, N, K, B.ld, BK);
+  else rc = make_map(tb, B.ptr, dtype, K, N, B.ld, BN / pair);
+  return rc;
+}
+
+void set_tiles(gemm::Params& p, int64_t M, int64_t N, int64_t K, int pair) {
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.num_m = (int)((M + BM * pair - 1) / (BM * pair));
+  p.num_n = (int)((N + BN - 1) / BN);
+  p.num_tiles = p.num_m * p.num_n;
 }
 
 // Generic: D[M,N] = scale * A B^T (+ addend), D written as out_dtype with pitch ldo.
@@ -119,21 +184,12 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
              const float* scale, int raster, int max_ctas, cudaStream_t st, int* status) {
   if (M <= 0 || N <= 0) return GH_OK;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return set_error(GH_EINVAL, "GEMM dimension too large");
+  const int pair = pick_pair(M);
   CUtensorMap ta, tb;
-  int rc;
-  if (A.mn_major) rc = make_map(&ta, A.ptr, dtype, M, K, A.ld, BK);
-  else rc = make_map(&ta, A.ptr, dtype, K, M, A.ld, BM);
-  if (rc) return rc;
-  if (B.mn_major) rc = make_map(&tb, B.ptr, dtype, N, K, B.ld, BK);
-  else rc = make_map(&tb, B.ptr, dtype, K, N, B.ld, BN);
+  int rc = make_operand_maps(&ta, &tb, dtype, A, B, M, N, K, pair);
   if (rc) return rc;
   gemm::Params p{};
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K = (int)K;
-  p.num_m = (int)((M + BM - 1) / BM);
-  p.num_n = (int)((N + BN - 1) / BN);
-  p.num_tiles = p.num_m * p.num_n;
+  set_tiles(p, M, N, K, pair);
   p.raster = raster;
   p.out = out;
   p.ldo = ldo;
@@ -146,13 +202,12 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
   p.ldadd = ldadd;
   p.scale = scale;
   p.status = status;
-  if (max_ctas <= 0) max_ctas = num_sms_dev();
   if (dtype == GH_BF16) {
-    if (out_dtype == GH_F32) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
-    if (out_dtype == GH_BF16) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
+    if (out_dtype == GH_F32) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
+    if (out_dtype == GH_BF16) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
   } else if (dtype == GH_F16) {
-    if (out_dtype == GH_F32) return launch_gemm_mm<__half, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
-    if (out_dtype == GH_F16) return launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, p, max_ctas, st);
+    if (out_dtype == GH_F32) return launch_gemm_mm<__half, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
+    if (out_dtype == GH_F16) return launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
   }
   return set_error(GH_ETYPE, "unsupported GEMM dtype combination (%d -> %d)", dtype, out_dtype);
 }
@@ -290,16 +345,12 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
     const int64_t* tc = target + s0;
     // 1. logits GEMM + fused CE statistics
     {
+      const int pair = pick_pair(rows);
       CUtensorMap ta, tb;
-      if ((rc = make_map(&ta, Hc, dtype, D, rows, D, BM))) return rc;
-      if ((rc = make_map(&tb, W, dtype, D, V, D, BN))) return rc;
+      if ((rc = make_operand_maps(&ta, &tb, dtype, Operand{Hc, D, 0}, Operand{W, D, 0}, rows, V, D, pair)))
+        return rc;
       gemm::Params p{};
-      p.M = (int)rows;
-      p.N = (int)V;
-      p.K = (int)D;
-      p.num_m = (int)((rows + BM - 1) / BM);
-      p.num_n = L.num_n;
-      p.num_tiles = p.num_m * p.num_n;
+      set_tiles(p, rows, V, D, pair);
       p.raster = 0;  // m fastest: concurrent CTAs share one W band, H stays in L2
       p.out = logits;
       p.ldo = L.ldl;
@@ -308,7 +359,9 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       p.stats = stats;
       p.xt = xt;
       p.status = status;
-      if ((rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T>(ta, tb, p, sms, st))) return rc;
+      if (pair == 2) rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 2>(ta, tb, p, sms, st);
+      else rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 1>(ta, tb, p, sms, st);
+      if (rc) return rc;
     }
     // 2. per-row logsumexp and loss terms
     lce_combine_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(stats, L.num_n, rows, xt, tc, V, ignore, lse,
@@ -318,11 +371,12 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
     if (!with_grad) continue;
     // 3. dlogits in place
     if ((rc = lce_dlogits<T>(logits, L.ldl, tc, lse, rows, V, zmul, ignore, sp, st))) return rc;
-    // 4. dW[D, V] (+)= H_c^T @ dlogits_c
+    // 4. dW[V, D] (+)= dlogits_c^T @ H_c  (row-major [V, D] = the op's [D, V]
+    //    gradient as a transposed view, so autograd can hand it to W.grad as is)
     if (grad_weight) {
       const bool first = c == 0, last = c == nchunks - 1;
-      Operand A{Hc, D, 1};
-      Operand B{logits, L.ldl, 1};
+      Operand A{logits, L.ldl, 1};
+      Operand B{Hc, D, 1};
       void* out;
       int out_dtype;
       const float* add_f32 = nullptr;
@@ -336,7 +390,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
         out_dtype = dtype;
         add_same = first ? nullptr : grad_weight;
       }
-      if ((rc = run_gemm(dtype, A, B, D, V, rows, out, out_dtype, V, add_f32, add_same, V, nullptr, 0, sms, st,
+      if ((rc = run_gemm(dtype, A, B, V, D, rows, out, out_dtype, D, add_f32, add_same, D, nullptr, 1, sms, st,
                          status)))
         return rc;
     }

@@ -7,7 +7,7 @@
 // cross-entropy:
 //   logits  = H @ W^T        A = H [C, D] K-major,        B = W [V, D] K-major
 //   dH      = dlogits @ W    A = dlogits [C, V] K-major,  B = W [V, D] MN-major
-//   dW^T    = H^T @ dlogits  A = H [C, D] MN-major,       B = dlogits [C, V] MN-major
+//   dW      = dlogits^T @ H  A = dlogits [C, V] MN-major, B = H [C, D] MN-major
 //
 // CTA: 256 threads, one CTA per SM, persistent over output tiles of
 // 128 x 256 (static round-robin over a rasterised tile order).
@@ -38,19 +38,14 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;           // 64 x 2 B = one 128-byte swizzle row
-constexpr int STAGES = 4;
 constexpr int THREADS = 256;
-constexpr int A_STAGE_BYTES = BM * BK * 2;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK * 2;  // 32 KB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 enum Epi { EPI_STORE = 0, EPI_LCE = 1 };
 
 struct Params {
   int M, N, K;
-  int num_m, num_n, num_tiles;
+  int num_m, num_n, num_tiles;   // num_m counts tiles of Geo<PAIR>::TM rows
   int raster;           // 0: m-tile fastest, 1: n-tile fastest
   // EPI_STORE
   void* out;
@@ -121,31 +116,50 @@ __device__ __forceinline__ void load_row32(const OutT* src, int col0, int N, flo
   }
 }
 
-template <typename T, int A_MN, int B_MN, int EPI, typename OutT>
+// Geometry of one configuration. PAIR = 1: one CTA computes a 128 x 256 tile.
+// PAIR = 2: a 2-CTA cluster computes a 256 x 256 tile with tcgen05.mma
+// cta_group::2; each CTA stages its 128 rows of A and 128 of the 256 B rows,
+// and holds its 128 accumulator rows in its own TMEM.
+template <int PAIR>
+struct Geo {
+  static constexpr int TM = BM * PAIR;            // tile rows
+  static constexpr int B_ROWS = BN / PAIR;        // B rows staged per CTA
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static constexpr int STG = PAIR == 2 ? 6 : 4;   // pipeline depth
+  static constexpr int SMEM = STG * (A_BYTES + B_BYTES) + 1024 + 256;
+};
+
+template <typename T, int A_MN, int B_MN, int EPI, typename OutT, int PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using G = Geo<PAIR>;
+  constexpr int STG = G::STG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* sB = smem + STG * G::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STG * G::B_BYTES);
+  uint64_t* empty = full + STG;
+  uint64_t* tfull = empty + STG;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR == 2 ? tc::cluster_ctarank() : 0;
+  const int unit = blockIdx.x / PAIR;         // cluster index
+  const int nunits = gridDim.x / PAIR;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < STG; ++s) {
       tc::mbar_init(&full[s], 1);
       tc::mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
-      tc::mbar_init(&tempty[b], 4);
+      tc::mbar_init(&tempty[b], 4 * PAIR);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -154,48 +168,73 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc::tma_prefetch_desc(&tmA);
     tc::tma_prefetch_desc(&tmB);
   }
-  if (warp == 2) tc::tmem_alloc(tmem_holder, TMEM_COLS);
+  if (warp == 2) {
+    if (PAIR == 2) tc::tmem_alloc_pair(tmem_holder, TMEM_COLS);
+    else tc::tmem_alloc(tmem_holder, TMEM_COLS);
+  }
   __syncthreads();
+  if (PAIR == 2) tc::cluster_sync();  // peer barriers initialised before any remote arrive
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int nkb = (p.K + BK - 1) / BK;
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
+      // ---------------- TMA producer (both CTAs of a pair) ----------------
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = unit; tile < p.num_tiles; tile += nunits) {
         int mt, nt;
         tile_coords(p, tile, mt, nt);
-        const int m0 = mt * BM, n0 = nt * BN;
+        const int ma = mt * G::TM + (int)rank * BM;         // this CTA's A rows
+        const int nb = nt * BN + (int)rank * G::B_ROWS;     // this CTA's B rows
         for (int kb = 0; kb < nkb; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) goto producer_done;
-          tc::mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          uint8_t* a = sA + stage * A_STAGE_BYTES;
-          uint8_t* b = sB + stage * B_STAGE_BYTES;
+          uint8_t* a = sA + stage * G::A_BYTES;
+          uint8_t* b = sB + stage * G::B_BYTES;
           const int k0 = kb * BK;
-          if (A_MN) {
+          if (PAIR == 1) {
+            tc::mbar_arrive_expect_tx(&full[stage], G::A_BYTES + G::B_BYTES);
+            if (A_MN) {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(a + j * (BK * 128), &tmA, &full[stage], m0 + j * 64, k0);
-          } else {
-            tc::tma_load_2d(a, &tmA, &full[stage], k0, m0);
-          }
-          if (B_MN) {
+              for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(a + j * (BK * 128), &tmA, &full[stage], ma + j * 64, k0);
+            } else {
+              tc::tma_load_2d(a, &tmA, &full[stage], k0, ma);
+            }
+            if (B_MN) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tc::tma_load_2d(b + j * (BK * 128), &tmB, &full[stage], n0 + j * 64, k0);
+              for (int j = 0; j < G::B_ROWS / 64; ++j)
+                tc::tma_load_2d(b + j * (BK * 128), &tmB, &full[stage], nb + j * 64, k0);
+            } else {
+              tc::tma_load_2d(b, &tmB, &full[stage], k0, nb);
+            }
           } else {
-            tc::tma_load_2d(b, &tmB, &full[stage], k0, n0);
+            // both CTAs' copies complete on the leader's full barrier
+            if (rank == 0) tc::mbar_arrive_expect_tx(&full[stage], 2 * (G::A_BYTES + G::B_BYTES));
+            const uint32_t fb = tc::mapa_shared(tc::smem_u32(&full[stage]), 0);
+            if (A_MN) {
+#pragma unroll
+              for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d_pair(a + j * (BK * 128), &tmA, fb, ma + j * 64, k0);
+            } else {
+              tc::tma_load_2d_pair(a, &tmA, fb, k0, ma);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < G::B_ROWS / 64; ++j)
+                tc::tma_load_2d_pair(b + j * (BK * 128), &tmB, fb, nb + j * 64, k0);
+            } else {
+              tc::tma_load_2d_pair(b, &tmB, fb, k0, nb);
+            }
           }
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == STG) { stage = 0; phase ^= 1; }
         }
       }
     producer_done:;
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = tc::instr_desc_f16(AbType<T>::v, A_MN, B_MN, BM, BN);
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (pair leader) ----------------
+      constexpr uint32_t idesc = tc::instr_desc_f16(AbType<T>::v, A_MN, B_MN, G::TM, BN);
       // K-major: 8-row groups of 128 B rows at 1024 B; K step of 16 = +32 B.
       // MN-major: 64-element column blocks at BK*128 B (LBO); K groups of 8
       // rows at 1024 B (SBO); K step of 16 = +2048 B.
@@ -206,7 +245,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      for (int tile = unit; tile < p.num_tiles; tile += nunits) {
         if (!tc::mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -214,31 +253,36 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int kb = 0; kb < nkb; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
           tc::tc_fence_after();
-          const uint32_t a0 = tc::smem_u32(sA + stage * A_STAGE_BYTES);
-          const uint32_t b0 = tc::smem_u32(sB + stage * B_STAGE_BYTES);
+          const uint32_t a0 = tc::smem_u32(sA + stage * G::A_BYTES);
+          const uint32_t b0 = tc::smem_u32(sB + stage * G::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t ad = tc::smem_desc_sw128(a0 + k * a_kstep, a_lbo, a_sbo);
             const uint64_t bd = tc::smem_desc_sw128(b0 + k * b_kstep, b_lbo, b_sbo);
-            tc::mma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            if (PAIR == 2) tc::mma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            else tc::mma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0);
           }
-          tc::mma_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (PAIR == 2) tc::mma_commit_pair_mc(&empty[stage], 0x3);
+          else tc::mma_commit(&empty[stage]);
+          if (++stage == STG) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        tc::mma_commit(&tfull[acc]);
+        if (PAIR == 2) tc::mma_commit_pair_mc(&tfull[acc], 0x3);
+        else tc::mma_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
   } else if (warp >= 4) {
     // ---------------- epilogue ----------------
     const int q = warp - 4;  // TMEM lane quarter this warp may access
+    const uint32_t tempty_leader0 = tc::mapa_shared(tc::smem_u32(&tempty[0]), 0);
+    const uint32_t tempty_leader1 = tc::mapa_shared(tc::smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+    for (int tile = unit; tile < p.num_tiles; tile += nunits) {
       int mt, nt;
       tile_coords(p, tile, mt, nt);
-      const int m0 = mt * BM, n0 = nt * BN;
+      const int m0 = mt * G::TM + (int)rank * BM, n0 = nt * BN;
       if (!tc::mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc::tc_fence_after();
       const int row = m0 + q * 32 + lane;
@@ -287,37 +331,43 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           tc::tmem_ld32(tbase + c * 32, r);
           tc::tmem_ld_wait();
           const int col0 = n0 + c * 32;
-          if (!row_ok || col0 >= p.N) continue;
-          float v[32];
+          if (row_ok && col0 < p.N) {
+            float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
-          if (p.add_f32) {
-            float a[32];
-            load_row32<float>(p.add_f32 + (int64_t)row * p.ldadd, col0, p.N, a, p.vec_ok);
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+            if (p.add_f32) {
+              float a[32];
+              load_row32<float>(p.add_f32 + (int64_t)row * p.ldadd, col0, p.N, a, p.vec_ok);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += a[j];
-          } else if (p.add_same) {
-            float a[32];
-            load_row32<OutT>(reinterpret_cast<const OutT*>(p.add_same) + (int64_t)row * p.ldadd, col0, p.N, a,
-                             p.vec_ok);
+              for (int j = 0; j < 32; ++j) v[j] += a[j];
+            } else if (p.add_same) {
+              float a[32];
+              load_row32<OutT>(reinterpret_cast<const OutT*>(p.add_same) + (int64_t)row * p.ldadd, col0, p.N, a,
+                               p.vec_ok);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] += a[j];
+              for (int j = 0; j < 32; ++j) v[j] += a[j];
+            }
+            store_row32<OutT>(orow, col0, p.N, v, p.vec_ok);
           }
-          store_row32<OutT>(orow, col0, p.N, v, p.vec_ok);
         }
       }
-      // release this accumulator buffer to the MMA warp
+      // release this accumulator buffer to the (leader's) MMA warp
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (PAIR == 2) tc::mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        else tc::mbar_arrive(&tempty[acc]);
+      }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }
   __syncthreads();
+  if (PAIR == 2) tc::cluster_sync();  // no CTA leaves while its peer may still signal it
   if (threadIdx.x == 0 && *abort_flag && p.status) atomicOr(p.status, 4);
   if (warp == 2) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR == 2) tc::tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tc::tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 

@@ -88,7 +88,8 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
     z_sum = torch.empty((), dtype=torch.float32, device=dev)
     n_valid = torch.empty((), dtype=torch.float32, device=dev)
     gi = torch.empty((B, D), dtype=inputs.dtype, device=dev) if with_grad else None
-    gw = torch.empty((D, V), dtype=weight.dtype, device=dev) if with_grad else None
+    # [V, D] row-major; returned as the [D, V] view (see _fake in the ops layer)
+    gw = torch.empty((V, D), dtype=weight.dtype, device=dev) if with_grad else None
     gs = grad_scale.reshape(1).float().contiguous() if grad_scale is not None else None
     defer = with_grad and grad_weight_hook is not None and B > 0
     stream = _lib.stream_of(inputs)
@@ -115,7 +116,7 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
         w_ = grad_weight_hook(gw)
         if w_ is not None:
             w_.wait()
-    return ce_sum, z_sum, n_valid, gi, gw
+    return ce_sum, z_sum, n_valid, gi, (gw.T if gw is not None else None)
 
 
 def linear_cross_entropy_with_grad(
@@ -130,6 +131,10 @@ def linear_cross_entropy_with_grad(
     grad_weight_hook=None,
 ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
     """Returns ``(ce_sum, z_sum, n_valid, grad_input [B, D], grad_weight [D, V])``.
+
+    ``grad_weight`` is the transposed view of a row-major ``[V, D]`` tensor:
+    the layout of ``W.grad`` for the ``[V, D]`` parameter the functional API
+    takes, so autograd accumulates it without a re-layout copy.
 
     With ``mean_reduction`` both gradients are already divided by
     ``max(n_valid, 1)``; ``grad_scale`` (1-element fp32 device tensor)
@@ -151,7 +156,7 @@ def linear_cross_entropy_with_grad(
     n_valid = torch.zeros((), dtype=torch.float32, device=dev)
     grad_input = torch.empty_like(inputs)
     acc_dtype = torch.float32 if fp32_grad_weight_accum else weight.dtype
-    grad_weight_acc = torch.zeros((D, V), dtype=acc_dtype, device=dev)
+    grad_weight_acc = torch.zeros((V, D), dtype=acc_dtype, device=dev)
     scale = grad_scale.reshape(1).float() if grad_scale is not None else None
     if mean_reduction:
         m = 1.0 / (target != ignore_index).sum().float().clamp(min=1.0).reshape(1)
@@ -167,12 +172,13 @@ def linear_cross_entropy_with_grad(
         z_sum += z
         n_valid += n
         grad_input[s:e] = logits @ weight.T
-        torch.addmm(grad_weight_acc, x.T, logits, out=grad_weight_acc, out_dtype=acc_dtype)
-    grad_weight = grad_weight_acc.to(weight.dtype)
+        torch.addmm(grad_weight_acc, logits.T, x, out=grad_weight_acc, out_dtype=acc_dtype)
+    grad_weight_vd = grad_weight_acc.to(weight.dtype)
     if grad_weight_hook is not None:
-        work = grad_weight_hook(grad_weight)
+        work = grad_weight_hook(grad_weight_vd)
         if work is not None:
             work.wait()
+    grad_weight = grad_weight_vd.T
     return ce_sum, z_sum, n_valid, grad_input, grad_weight
 
 

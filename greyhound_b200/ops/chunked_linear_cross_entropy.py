@@ -9,7 +9,11 @@ its fake (:70-88), the forward-only fast path (:91-132) and
 ``ctx.needs_input_grad`` gate (:150) and gradients computed in the forward and
 scaled by ``grad_output`` in the backward.
 
-B200 difference (results unchanged within tolerance): for ``reduction="mean"``
+B200 differences (results unchanged within tolerance): ``grad_weight`` is
+returned as the transposed view of a row-major ``[V, D]`` buffer (strides
+``(1, D)``) instead of a contiguous ``[D, V]`` tensor (:87), so ``W.grad`` of
+the ``[V, D]`` parameter is produced without a 1 GB re-layout copy; and for
+``reduction="mean"``
 the Function calls ``greyhound::chunked_linear_cross_entropy_fwd_mean``, which
 folds ``1 / max(n_valid, 1)`` into the logits gradient before the two
 gradient GEMMs instead of two ``mul_`` passes over ``grad_input`` and
@@ -44,7 +48,8 @@ def _fake(inputs: Tensor, weight: Tensor) -> tuple[Tensor, Tensor, Tensor, Tenso
         torch.empty([], dtype=torch.float32, device=inputs.device),
         torch.empty([], dtype=torch.float32, device=inputs.device),
         torch.empty([B, D], dtype=inputs.dtype, device=inputs.device),
-        torch.empty([D, V], dtype=weight.dtype, device=inputs.device),
+        # [D, V] gradient stored as a transposed [V, D] row-major buffer
+        torch.empty_strided([D, V], [1, D], dtype=weight.dtype, device=inputs.device),
     )
 
 

@@ -145,8 +145,10 @@ GH_API int gh_logits_grad(const void* logits, void* dlogits, const int64_t* labe
  *   chunk_rows: rows per chunk (<= 0: all rows in one chunk); the logits of
  *          one chunk ([chunk, V] in the activation dtype) live in the workspace
  *   grad_input  [N, D] (same dtype) or NULL
- *   grad_weight [D, V] (same dtype, the layout of the reference op's output)
- *          or NULL; both NULL -> loss only
+ *   grad_weight [V, D] row-major (same dtype) or NULL; both NULL -> loss
+ *          only. This is the reference op's [D, V] grad_weight stored
+ *          transposed, so the autograd layer can return it as the [D, V]
+ *          view and W.grad ([V, D]) needs no re-layout copy
  *   fp32_grad_weight_accum: 1 -> weight gradient accumulated across chunks in
  *          fp32 and cast once; 0 -> accumulated in the weight dtype
  *   mean_reduction / grad_scale: as for gh_ce_fwd_grad; the scale is folded
