@@ -62,8 +62,12 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _i64, _i32, _vp, _i64, _i32, _i64, _i64, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _vp, _vp, _vp],
     ),
+    "gh_scale": (_i32, [_vp, _vp, _i64, _i32, _vp, _vp]),
+    "gh_profile_enable": (None, [_i32]),
+    "gh_profile_read": (_i32, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong), _i32, _i32]),
 }
 GH_LCE_DEFER_LAST_DH = 1
+PROF_CLASSES = ("gemm_logits_ce", "gemm_dw", "gemm_dh", "dlogits", "rows", "gemm_other")
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
@@ -137,3 +141,29 @@ def device_status(ws: torch.Tensor) -> int:
     """Read the device status word of a workspace (synchronises the stream)."""
     off = int(load().gh_workspace_status_offset())
     return int(ws[off : off + 4].view(torch.int32).item())
+
+
+def profile_enable(on: bool) -> None:
+    load().gh_profile_enable(1 if on else 0)
+
+
+def profile_read(reset: bool = True) -> dict[str, tuple[float, int]]:
+    """{class: (total_ms, launches)} of the event-timed launches (synchronises)."""
+    n = len(PROF_CLASSES)
+    ms = (ctypes.c_double * n)()
+    cnt = (ctypes.c_longlong * n)()
+    check(load().gh_profile_read(ms, cnt, n, 1 if reset else 0), "profile_read")
+    return {PROF_CLASSES[i]: (ms[i], cnt[i]) for i in range(n)}
+
+
+def scaled(t: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+    """``t * g`` for a device scalar ``g`` (new tensor, same strides as ``t``)."""
+    if t.numel() == 0 or t.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        return t * g
+    if not (t.is_contiguous() or t.T.is_contiguous()) or t.data_ptr() % 16:
+        return t * g
+    out = torch.empty_like(t)  # preserves the (possibly transposed) dense layout
+    gf = g.detach().reshape(1).to(torch.float32)
+    check(load().gh_scale(t.data_ptr(), out.data_ptr(), t.numel(), dtype_code(t.dtype), gf.data_ptr(),
+                          stream_of(t)), "scale")
+    return out

@@ -25,6 +25,25 @@ int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 void count_launch(int n = 1);
 
+// Kernel classes for the optional event timing (gh_profile_enable / _read).
+enum ProfClass {
+  PROF_GEMM_LOGITS_CE = 0,  // logits GEMM with the fused CE epilogue
+  PROF_GEMM_DW = 1,
+  PROF_GEMM_DH = 2,
+  PROF_DLOGITS = 3,
+  PROF_ROWS = 4,            // standalone CE / SLS row kernels
+  PROF_GEMM_OTHER = 5,
+  PROF_NUM = 6
+};
+// RAII: records an event pair around the launches in its scope when timing is on.
+struct ProfScope {
+  ProfScope(int cls, cudaStream_t st);
+  ~ProfScope();
+  int cls_;
+  cudaStream_t st_;
+  void* a_;
+};
+
 inline int elt_size(int dtype) {
   switch (dtype) {
     case GH_F16: case GH_BF16: return 2;

@@ -181,8 +181,10 @@ void set_tiles(gemm::Params& p, int64_t M, int64_t N, int64_t K, int pair) {
 // Generic: D[M,N] = scale * A B^T (+ addend), D written as out_dtype with pitch ldo.
 int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N, int64_t K, void* out,
              int out_dtype, int64_t ldo, const float* add_f32, const void* add_same, int64_t ldadd,
-             const float* scale, int raster, int max_ctas, cudaStream_t st, int* status) {
+             const float* scale, int raster, int max_ctas, cudaStream_t st, int* status,
+             int prof_class = PROF_GEMM_OTHER) {
   if (M <= 0 || N <= 0) return GH_OK;
+  ProfScope prof(prof_class, st);
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return set_error(GH_EINVAL, "GEMM dimension too large");
   const int pair = pick_pair(M);
   CUtensorMap ta, tb;
@@ -307,6 +309,7 @@ int lce_dlogits(T* logits, int64_t ld, const int64_t* labels, const float* lse, 
   chunk = (chunk + per - 1) / per * per;
   s = (V + chunk - 1) / chunk;
   dim3 grid((unsigned)rows, (unsigned)s);
+  ProfScope prof(PROF_DLOGITS, st);
   lce_dlogits_kernel<T, 256><<<grid, 256, 0, st>>>(logits, ld, labels, lse, V, chunk, zmul, ignore, scale);
   count_launch(1);
   return check_launch("lce_dlogits");
@@ -359,6 +362,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       p.stats = stats;
       p.xt = xt;
       p.status = status;
+      ProfScope prof(PROF_GEMM_LOGITS_CE, st);
       if (pair == 2) rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 2>(ta, tb, p, sms, st);
       else rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 1>(ta, tb, p, sms, st);
       if (rc) return rc;
@@ -391,7 +395,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
         add_same = first ? nullptr : grad_weight;
       }
       if ((rc = run_gemm(dtype, A, B, V, D, rows, out, out_dtype, D, add_f32, add_same, D, nullptr, 1, sms, st,
-                         status)))
+                         status, PROF_GEMM_DW)))
         return rc;
     }
     // 5. dH rows [s0, s0 + rows) = dlogits_c @ W
@@ -399,7 +403,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       Operand A{logits, L.ldl, 0};
       Operand B{W, D, 1};
       if ((rc = run_gemm(dtype, A, B, rows, D, V, static_cast<T*>(grad_input) + s0 * D, dtype, D, nullptr, nullptr,
-                         0, nullptr, 1, sms, st, status)))
+                         0, nullptr, 1, sms, st, status, PROF_GEMM_DH)))
         return rc;
     }
   }
@@ -463,7 +467,8 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
   Operand B{W, D, 1};
   const int elt = elt_size(dtype);
   return run_gemm(dtype, A, B, rows, D, V, static_cast<char*>(grad_input) + s0 * D * elt, dtype, D, nullptr, nullptr,
-                  0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status));
+                  0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status),
+                  PROF_GEMM_DH);
 }
 
 extern "C" int gh_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,

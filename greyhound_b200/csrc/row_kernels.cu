@@ -305,6 +305,7 @@ int launch_ce(const void* logits, void* dlogits, const int64_t* labels, int64_t 
     ++launches;
   }
   const float* sp = (mean && y) ? scale : gscale;
+  ProfScope prof(PROF_ROWS, st);
   if (rows > 0) {
     if (p.fused) {
       int64_t grid = rows;
@@ -341,6 +342,7 @@ int launch_sls(const void* logits, const void* index, int64_t rows, int64_t V, v
   O* o = static_cast<O*>(out);
   cudaMemsetAsync(status, 0, sizeof(int), st);
   if (rows == 0) return check_launch("gh_sls_fwd");
+  ProfScope prof(PROF_ROWS, st);
   if (p.fused) {
     int64_t grid = rows;
     const int64_t cap = (int64_t)num_sms() * 2 * 64;
@@ -555,4 +557,51 @@ extern "C" int gh_logits_grad(const void* logits, void* dlogits, const int64_t* 
     case GH_F16: return launch_logits_grad<__half>(logits, dlogits, labels, lse, rows, vocab, z_loss_multiplier, ignore_index, label_offset, grad_scale, st);
     default: return launch_logits_grad<float>(logits, dlogits, labels, lse, rows, vocab, z_loss_multiplier, ignore_index, label_offset, grad_scale, st);
   }
+}
+
+// out[i] = in[i] * (*g): the backward of an op whose gradients were computed
+// in the forward (ops/*: grad * grad_output), vectorised, g read on the device.
+namespace gh {
+namespace {
+template <typename T>
+__global__ void __launch_bounds__(256) scale_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t n,
+                                                    const float* __restrict__ g) {
+  constexpr int PER = 16 / sizeof(T);
+  const float s = *g;
+  const int64_t nvec = n / PER;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    Vec16<T> v;
+    v.raw = ld16(reinterpret_cast<const uint4*>(in) + i);
+    float f[PER];
+    v.to_float(f);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) f[k] *= s;
+    v.from_float(f);
+    st16_cs(reinterpret_cast<uint4*>(out) + i, v.raw);
+  }
+  for (int64_t i = nvec * PER + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    out[i] = Elt<T>::from_f(Elt<T>::to_f(in[i]) * s);
+}
+}  // namespace
+}  // namespace gh
+
+extern "C" int gh_scale(const void* in, void* out, int64_t n, int dtype, const float* g, void* stream) {
+  if (!is_float_dtype(dtype)) return set_error(GH_ETYPE, "unsupported dtype code %d", dtype);
+  if (n < 0 || (n > 0 && (!in || !out || !g))) return set_error(GH_EINVAL, "bad arguments");
+  if (n == 0) return GH_OK;
+  if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(GH_EINVAL, "gh_scale needs 16-byte aligned buffers");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = num_sms();
+  int64_t blocks = (n / (16 / elt_size(dtype)) + 255) / 256;
+  if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
+  if (blocks < 1) blocks = 1;
+  switch (dtype) {
+    case GH_BF16: scale_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), n, g); break;
+    case GH_F16: scale_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __half*>(in), static_cast<__half*>(out), n, g); break;
+    default: scale_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const float*>(in), static_cast<float*>(out), n, g); break;
+  }
+  count_launch(1);
+  return check_launch("gh_scale");
 }

@@ -28,6 +28,7 @@ import torch
 import torch.distributed as dist
 from torch import Tensor
 
+from greyhound_b200.ops.scale import scale_by
 from greyhound_b200.kernels import linear_cross_entropy as lce
 
 __all__ = [
@@ -81,7 +82,7 @@ class RowShardedLinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         gi, gw = ctx.saved_tensors
-        return gi * g, gw * g, None, None, None, None, None, None
+        return scale_by(gi, g), scale_by(gw, g), None, None, None, None, None, None
 
 
 def row_sharded_linear_cross_entropy(
@@ -159,7 +160,7 @@ class VocabShardedLinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         gi, gw = ctx.saved_tensors
-        return gi * g, gw * g, None, None, None, None, None, None
+        return scale_by(gi, g), scale_by(gw, g), None, None, None, None, None, None
 
 
 def vocab_sharded_linear_cross_entropy(

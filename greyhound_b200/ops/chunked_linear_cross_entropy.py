@@ -27,6 +27,7 @@ from typing import Literal
 import torch
 from torch import Tensor
 
+from greyhound_b200.ops.scale import scale_by
 from greyhound_b200.kernels.linear_cross_entropy import (
     linear_cross_entropy_loss,
     linear_cross_entropy_with_grad,
@@ -191,8 +192,8 @@ class ChunkedLinearCrossEntropyFunction(torch.autograd.Function):
     def backward(ctx: object, grad_output: Tensor):  # type: ignore[override]
         grad_input, grad_weight, _ = ctx.saved_tensors  # type: ignore[attr-defined]
         return (
-            grad_input * grad_output,
-            grad_weight * grad_output,
+            scale_by(grad_input, grad_output),
+            scale_by(grad_weight, grad_output),
             None,
             None,
             None,

@@ -14,6 +14,7 @@ from collections.abc import Callable
 import torch
 from torch import Tensor
 
+from greyhound_b200.ops.scale import scale_by
 from greyhound_b200.kernels.linear_cross_entropy import chunk_size_for
 
 __all__ = ["ChunkedLinearLossFunction"]
@@ -114,4 +115,4 @@ class ChunkedLinearLossFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx: object, grad_output: Tensor):  # type: ignore[override]
         grad_input, grad_weight = ctx.saved_tensors  # type: ignore[attr-defined]
-        return grad_input * grad_output, grad_weight * grad_output, None, None, None
+        return scale_by(grad_input, grad_output), scale_by(grad_weight, grad_output), None, None, None

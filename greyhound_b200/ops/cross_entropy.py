@@ -19,6 +19,7 @@ from typing import Any, Literal
 import torch
 from torch import Tensor
 
+from greyhound_b200.ops.scale import scale_by
 from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad
 
 __all__ = ["CrossEntropyFunction", "cross_entropy_fwd", "cross_entropy_fwd_mean"]
@@ -113,4 +114,4 @@ class CrossEntropyFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx: Any, grad_output: Tensor) -> tuple[Tensor, None, None, None, None]:  # type: ignore[override]
         (grad_logits,) = ctx.saved_tensors
-        return grad_logits * grad_output, None, None, None, None
+        return scale_by(grad_logits, grad_output), None, None, None, None

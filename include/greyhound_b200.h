@@ -194,6 +194,22 @@ GH_API int gh_gemm(const void* A, int64_t lda, int a_mn_major,
                    const void* addend, int64_t ld_add, const float* scale,
                    int* status, void* stream);
 
+/* ------------------------------------------------------------------------ *
+ * out[i] = in[i] * (*g) for n elements (F16 / BF16 / F32), g a device float.
+ * The backward of the ops whose gradients are computed in the forward
+ * (src/greyhound/ops/chunked_linear_cross_entropy.py:175-185,
+ * ops/cross_entropy.py:79-85: saved_grad * grad_output) without a host sync
+ * and without torch's mixed-dtype broadcast path. 16-byte aligned buffers.
+ * ------------------------------------------------------------------------ */
+GH_API int gh_scale(const void* in, void* out, int64_t n, int dtype, const float* g, void* stream);
+
+/* Optional event timing of the library's launches, by kernel class:
+ * 0 logits GEMM + fused CE epilogue, 1 dW GEMM, 2 dH GEMM, 3 dlogits pass,
+ * 4 standalone row kernels, 5 other GEMMs. gh_profile_read synchronises on
+ * the recorded events and returns total ms and launch count per class. */
+GH_API void gh_profile_enable(int on);
+GH_API int gh_profile_read(double* ms_out, long long* count_out, int n_classes, int reset);
+
 #ifdef __cplusplus
 }
 #endif
