@@ -47,6 +47,11 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _vp, _vp, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
+    "gh_ce_noalloc_scratch_bytes": (_sz, []),
+    "gh_ce_fwd_grad_noalloc": (
+        _i32,
+        [_vp, _vp, _vp, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _vp, _vp, _vp, _vp, _vp],
+    ),
     "gh_sls_workspace_bytes": (_sz, [_i64, _i64, _i32]),
     "gh_sls_fwd": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _vp, _i32, _vp, _vp, _sz, _vp]),
     "gh_sls_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i64, _i64, _i32, _vp, _vp]),

@@ -20,6 +20,8 @@
 //     the label logit, a second kernel merges them and writes the gradient.
 // Per-row loss terms go to workspace arrays; one single-CTA kernel sums them
 // in a fixed order, so results are bit-reproducible run to run.
+#include <mutex>
+
 #include "common.cuh"
 #include "row_ops.cuh"
 
@@ -604,4 +606,66 @@ extern "C" int gh_scale(const void* in, void* out, int64_t n, int dtype, const f
   }
   count_launch(1);
   return check_launch("gh_scale");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of gh_ce_fwd_grad.
+//
+// Some callers cannot allocate device memory at all at the point where they
+// need the loss: code running under an allocator that forbids it, custom
+// runtimes with their own pool that does not hand out scratch, or a host
+// language binding with no device allocator of its own. For them the scratch
+// lives in a fixed, library-owned device array instead of a caller workspace.
+// Every GPU that loads this library holds the array (GH_CE_NOALLOC_SCRATCH_BYTES)
+// until the process exits.
+namespace gh {
+namespace {
+constexpr size_t kNoAllocScratchBytes = 4u << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_ce_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the scratch array for the current device. The array's
+// host-side name is only a stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(GH_EUNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ce_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(GH_ECUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return GH_OK;
+}
+}  // namespace
+}  // namespace gh
+
+extern "C" size_t gh_ce_noalloc_scratch_bytes(void) { return gh::kNoAllocScratchBytes; }
+
+extern "C" int gh_ce_fwd_grad_noalloc(const void* logits, void* dlogits, const int64_t* labels, int64_t rows,
+                                      int64_t vocab, int dtype, float z_loss_multiplier, int64_t ignore_index,
+                                      int mean_reduction, const float* grad_scale, float* ce_sum, float* z_sum,
+                                      float* n_valid, float* lse_out, void* stream) {
+  const size_t need = gh_ce_workspace_bytes(rows, vocab, dtype);
+  if (need == 0 && (!is_float_dtype(dtype)))
+    return set_error(GH_ETYPE, "unsupported logits dtype code %d", dtype);
+  if (need > kNoAllocScratchBytes)
+    return set_error(GH_EINVAL,
+                     "gh_ce_fwd_grad_noalloc: %lld rows x %lld vocab need %zu scratch bytes, more than the "
+                     "fixed %zu; use gh_ce_fwd_grad with a caller workspace",
+                     (long long)rows, (long long)vocab, need, kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return gh_ce_fwd_grad(logits, dlogits, labels, rows, vocab, dtype, z_loss_multiplier, ignore_index,
+                        mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, scratch,
+                        kNoAllocScratchBytes, stream);
 }

@@ -94,6 +94,25 @@ GH_API int gh_ce_fwd_grad(const void* logits, void* dlogits, const int64_t* labe
                    float* ce_sum, float* z_sum, float* n_valid, float* lse_out,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of gh_ce_fwd_grad (no counterpart in the reference).
+ * For callers that cannot allocate device memory where they need the loss
+ * (a forbidding allocator, a runtime whose pool offers no scratch, a binding
+ * without a device allocator): the scratch is a fixed library-owned device
+ * array of gh_ce_noalloc_scratch_bytes() (4 MiB) that every GPU loading the
+ * library holds until exit. Shapes whose scratch would exceed it are rejected
+ * with GH_EINVAL (about 349,000 rows at any vocab size). The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture). All calls share the array, so calls that overlap on the GPU
+ * (concurrent streams) race; serialise them. Arguments and results as
+ * gh_ce_fwd_grad. */
+GH_API size_t gh_ce_noalloc_scratch_bytes(void);
+GH_API int gh_ce_fwd_grad_noalloc(const void* logits, void* dlogits, const int64_t* labels,
+                                  int64_t rows, int64_t vocab, int dtype,
+                                  float z_loss_multiplier, int64_t ignore_index,
+                                  int mean_reduction, const float* grad_scale,
+                                  float* ce_sum, float* z_sum, float* n_valid, float* lse_out,
+                                  void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Selective log-softmax: out[r] = logits[r, index[r]] - logsumexp(logits[r]).
  * Replaces selective_log_softmax_kernel(logits, index)  kernels/logprobs.py:131
