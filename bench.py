@@ -388,20 +388,20 @@ def bench_rows(args, rank, world, local, which):
     g = torch.Generator(device=dev)
     g.manual_seed(1 + rank)
     if which == "ce":
-        rows, V = 4096, 128256
+        rows, V = args.rows or 4096, args.vocab or 128256
         x = (torch.randn(rows, V, device=dev, generator=g) * 2).to(torch.bfloat16)
         t = torch.randint(0, V, (rows,), device=dev, generator=g)
         out = torch.empty_like(x)
         step = lambda: cross_entropy_with_grad(x, t, 0.0, -100, out, mean_reduction=True)  # noqa: E731
         nbytes = 2 * rows * V * 2 + rows * 8
-        metric = "cross_entropy fwd+grad GB/s [4096,128256] bf16"
+        metric = f"cross_entropy fwd+grad GB/s [{rows},{V}] bf16"
     else:
-        rows, V = 65536, 151936
+        rows, V = args.rows or 65536, args.vocab or 151936
         x = (torch.randn(rows, V, device=dev, generator=g) * 3).to(torch.bfloat16)
         t = torch.randint(0, V, (rows,), device=dev, generator=g)
         step = lambda: selective_log_softmax_with_lse(x, t, out_dtype=torch.float32)  # noqa: E731
         nbytes = rows * V * 2 + rows * 8 + rows * 4
-        metric = "selective_log_softmax fwd GB/s [65536,151936] bf16"
+        metric = f"selective_log_softmax fwd GB/s [{rows},{V}] bf16"
     c0 = _lib.launch_count()
     with ClockSampler(local) as clk:
         ms = time_steps(step, args.steps, args.warmup, world)
