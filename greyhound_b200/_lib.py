@@ -68,6 +68,12 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i32, _vp, _i64, _i32, _i64, _i64, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _vp, _vp, _vp],
     ),
     "gh_scale": (_i32, [_vp, _vp, _i64, _i32, _vp, _vp]),
+    "gh_lce_shard_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
+    "gh_lce_shard_stats": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _sz, _vp]),
+    "gh_lce_shard_grads": (
+        _i32,
+        [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp],
+    ),
     "gh_profile_enable": (None, [_i32]),
     "gh_profile_read": (_i32, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong), _i32, _i32]),
 }
@@ -163,6 +169,8 @@ def profile_read(reset: bool = True) -> dict[str, tuple[float, int]]:
 
 def scaled(t: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
     """``t * g`` for a device scalar ``g`` (new tensor, same strides as ``t``)."""
+    if not t.is_cuda:
+        raise ValueError("expected a CUDA tensor (greyhound_b200 has no CPU path)")
     if t.numel() == 0 or t.dtype not in (torch.float16, torch.bfloat16, torch.float32):
         return t * g
     if not (t.is_contiguous() or t.T.is_contiguous()) or t.data_ptr() % 16:

@@ -218,22 +218,43 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
 // Linear-CE helper kernels
 
 // Exact per-row logsumexp from the epilogue's per-tile (max, sum) pairs and
-// the per-row loss terms (kernels/cross_entropy.py:84-92).
-__global__ void __launch_bounds__(256)
+// the per-row loss terms (kernels/cross_entropy.py:84-92). Block = 32 rows x
+// 8 warps: lane <-> row (coalesced reads of the [tile][row] partials), warps
+// split the tiles, then one merge across warps.
+// shard mode (stats3 != nullptr): rows hold only a vocab shard; write
+// (lse_shard, 1, target logit or -inf) for the cross-shard exchange instead of
+// loss terms.
+constexpr int kCombineWarps = 8;
+__global__ void __launch_bounds__(32 * kCombineWarps)
 lce_combine_kernel(const float2* __restrict__ stats, int num_n, int64_t rows, const float* __restrict__ xt,
-                   const int64_t* __restrict__ labels, int64_t V, int64_t ignore, float* lse_out, float* row_ce,
-                   float* row_z, int* status) {
-  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= rows) return;
+                   const int64_t* __restrict__ labels, int64_t label_offset, int64_t V, int64_t ignore,
+                   float* lse_out, float* row_ce, float* row_z, float* stats3, int* status) {
+  __shared__ float sm[kCombineWarps][32], ss[kCombineWarps][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * 32 + lane;
   MS acc = ms_empty();
-  for (int j = 0; j < num_n; ++j) {
-    const float2 p = stats[(int64_t)j * rows + r];
-    acc = ms_merge(acc, MS{p.x, p.y});
-  }
+  if (r < rows)
+    for (int j = w; j < num_n; j += kCombineWarps) {
+      const float2 p = stats[(int64_t)j * rows + r];
+      acc = ms_merge(acc, MS{p.x, p.y});
+    }
+  sm[w][lane] = acc.m;
+  ss[w][lane] = acc.s;
+  __syncthreads();
+  if (w != 0 || r >= rows) return;
+  for (int k = 1; k < kCombineWarps; ++k) acc = ms_merge(acc, MS{sm[k][lane], ss[k][lane]});
   const float lse = (acc.m + fast_log2(acc.s)) * kLn2;
-  const int64_t lab = labels[r];
-  bool valid = lab != ignore;
-  if (valid && (lab < 0 || lab >= V)) {
+  const int64_t t = labels[r];
+  const int64_t loc = t - label_offset;
+  if (stats3) {
+    const bool inside = t != ignore && loc >= 0 && loc < V;
+    stats3[3 * r + 0] = lse;
+    stats3[3 * r + 1] = 1.f;
+    stats3[3 * r + 2] = inside ? xt[r] : kNegInf;
+    return;
+  }
+  bool valid = t != ignore;
+  if (valid && (loc < 0 || loc >= V)) {
     atomicOr(status, GH_DEV_BAD_LABEL);
     valid = false;
   }
@@ -243,24 +264,29 @@ lce_combine_kernel(const float2* __restrict__ stats, int num_n, int64_t rows, co
 }
 
 // In-place logits -> dlogits over a pitched [rows, ld] buffer; grid (rows, chunks).
+// Rows with target == ignore get zeros. In shard mode the one-hot term is only
+// subtracted when the target falls in this shard's columns; otherwise a target
+// outside [0, V) marks a bad label (zero row, flagged by the combine kernel).
 template <typename T, int THREADS>
 __global__ void __launch_bounds__(THREADS)
-lce_dlogits_kernel(T* logits, int64_t ld, const int64_t* __restrict__ labels, const float* __restrict__ lse,
-                   int64_t V, int64_t chunk, float zmul, int64_t ignore, const float* scale_ptr) {
+lce_dlogits_kernel(T* logits, int64_t ld, const int64_t* __restrict__ labels, int64_t label_offset, int shard,
+                   const float* __restrict__ lse, int64_t V, int64_t chunk, float zmul, int64_t ignore,
+                   const float* scale_ptr) {
   const int64_t row = blockIdx.x;
   const int64_t c0 = (int64_t)blockIdx.y * chunk;
   if (c0 >= V) return;
   const int64_t n = c0 + chunk < V ? chunk : V - c0;
-  const int64_t lab = labels[row];
+  const int64_t t = labels[row];
+  const int64_t loc = t - label_offset;
   T* y = logits + row * ld + c0;
-  if (lab == ignore || lab < 0 || lab >= V) {
+  if (t == ignore || (!shard && (loc < 0 || loc >= V))) {
     row_zero<T, THREADS>(y, n);
     return;
   }
   const float l = lse[row];
   const float scale = scale_ptr ? *scale_ptr : 1.f;
   const float coef = scale * (1.f + 2.f * zmul * l);
-  row_grad<T, THREADS, kUnroll>(y, y, n, lab - c0, l * kLog2e, coef, scale);
+  row_grad<T, THREADS, kUnroll>(y, y, n, loc - c0, l * kLog2e, coef, scale);
 }
 
 struct LceLayout {
@@ -297,7 +323,8 @@ LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, 
 
 template <typename T>
 int lce_dlogits(T* logits, int64_t ld, const int64_t* labels, const float* lse, int64_t rows, int64_t V,
-                float zmul, int64_t ignore, const float* scale, cudaStream_t st) {
+                float zmul, int64_t ignore, const float* scale, cudaStream_t st, int64_t label_offset = 0,
+                int shard = 0) {
   if (rows <= 0) return GH_OK;
   const int sms = num_sms_dev();
   int64_t want = (8 * (int64_t)sms + rows - 1) / rows;
@@ -310,7 +337,8 @@ int lce_dlogits(T* logits, int64_t ld, const int64_t* labels, const float* lse, 
   s = (V + chunk - 1) / chunk;
   dim3 grid((unsigned)rows, (unsigned)s);
   ProfScope prof(PROF_DLOGITS, st);
-  lce_dlogits_kernel<T, 256><<<grid, 256, 0, st>>>(logits, ld, labels, lse, V, chunk, zmul, ignore, scale);
+  lce_dlogits_kernel<T, 256><<<grid, 256, 0, st>>>(logits, ld, labels, label_offset, shard, lse, V, chunk, zmul,
+                                                   ignore, scale);
   count_launch(1);
   return check_launch("lce_dlogits");
 }
@@ -368,8 +396,8 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       if (rc) return rc;
     }
     // 2. per-row logsumexp and loss terms
-    lce_combine_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(stats, L.num_n, rows, xt, tc, V, ignore, lse,
-                                                                      row_ce + s0, row_z + s0, status);
+    lce_combine_kernel<<<(unsigned)((rows + 31) / 32), 32 * kCombineWarps, 0, st>>>(
+        stats, L.num_n, rows, xt, tc, 0, V, ignore, lse, row_ce + s0, row_z + s0, nullptr, status);
     count_launch(1);
     if ((rc = check_launch("lce_combine"))) return rc;
     if (!with_grad) continue;
@@ -410,6 +438,66 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
   ce_finalize_kernel<<<1, 1024, 0, st>>>(row_ce, row_z, target, N, ignore, ce_sum, z_sum, n_valid);
   count_launch(1);
   return check_launch("lce_finalize");
+}
+
+// ---------------------------------------------------------------------------
+// Vocab-parallel phases (one vocab shard of W per rank; all rows in one chunk).
+
+template <typename T>
+int shard_stats_run(const void* H, const void* W, const int64_t* target, int64_t N, int64_t D, int64_t Vs,
+                    int64_t vstart, int dtype, float* stats3, const LceLayout& L, char* ws, cudaStream_t st) {
+  int* status = reinterpret_cast<int*>(ws + L.status);
+  T* logits = reinterpret_cast<T*>(ws + L.logits);
+  float2* stats = reinterpret_cast<float2*>(ws + L.stats);
+  float* xt = reinterpret_cast<float*>(ws + L.xt);
+  cudaMemsetAsync(status, 0, sizeof(int), st);
+  const int pair = pick_pair(N);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_operand_maps(&ta, &tb, dtype, Operand{H, D, 0}, Operand{W, D, 0}, N, Vs, D, pair))) return rc;
+  gemm::Params p{};
+  set_tiles(p, N, Vs, D, pair);
+  p.raster = 0;
+  p.out = logits;
+  p.ldo = L.ldl;
+  p.vec_ok = ((L.ldl * (int64_t)sizeof(T)) & 15) == 0;
+  p.labels = target;
+  p.label_offset = vstart;
+  p.stats = stats;
+  p.xt = xt;
+  p.status = status;
+  {
+    ProfScope prof(PROF_GEMM_LOGITS_CE, st);
+    if (pair == 2) rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 2>(ta, tb, p, num_sms_dev(), st);
+    else rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 1>(ta, tb, p, num_sms_dev(), st);
+    if (rc) return rc;
+  }
+  lce_combine_kernel<<<(unsigned)((N + 31) / 32), 32 * kCombineWarps, 0, st>>>(
+      stats, L.num_n, N, xt, target, vstart, Vs, INT64_MIN, nullptr, nullptr, nullptr, stats3, status);
+  count_launch(1);
+  return check_launch("lce_shard_combine");
+}
+
+template <typename T>
+int shard_grads_run(const void* H, const void* W, const int64_t* target, const float* lse, int64_t N, int64_t D,
+                    int64_t Vs, int64_t vstart, int dtype, float zmul, int64_t ignore, const float* grad_scale,
+                    void* grad_input, void* grad_weight, const LceLayout& L, char* ws, cudaStream_t st) {
+  int* status = reinterpret_cast<int*>(ws + L.status);
+  T* logits = reinterpret_cast<T*>(ws + L.logits);
+  const int sms = num_sms_dev();
+  int rc;
+  if ((rc = lce_dlogits<T>(logits, L.ldl, target, lse, N, Vs, zmul, ignore, grad_scale, st, vstart, 1))) return rc;
+  if (grad_weight) {
+    if ((rc = run_gemm(dtype, Operand{logits, L.ldl, 1}, Operand{H, D, 1}, Vs, D, N, grad_weight, dtype, D, nullptr,
+                       nullptr, 0, nullptr, 1, sms, st, status, PROF_GEMM_DW)))
+      return rc;
+  }
+  if (grad_input) {
+    if ((rc = run_gemm(dtype, Operand{logits, L.ldl, 0}, Operand{W, D, 1}, N, D, Vs, grad_input, dtype, D, nullptr,
+                       nullptr, 0, nullptr, 1, sms, st, status, PROF_GEMM_DH)))
+      return rc;
+  }
+  return GH_OK;
 }
 
 }  // namespace
@@ -483,4 +571,47 @@ extern "C" int gh_gemm(const void* A, int64_t lda, int a_mn_major, const void* B
   const int raster = M >= N ? 1 : 0;
   return run_gemm(dtype, a, b, M, N, K, out, out_dtype, ldo, add_f32, add_same, ld_add, scale, raster, 0,
                   static_cast<cudaStream_t>(stream), status);
+}
+
+extern "C" size_t gh_lce_shard_workspace_bytes(int64_t N, int64_t D, int64_t V_shard, int dtype) {
+  if (N < 0 || D <= 0 || V_shard <= 0 || elt_size(dtype) != 2) return 0;
+  return lce_layout(N, D, V_shard, N, dtype, 0).total;
+}
+
+extern "C" int gh_lce_shard_stats(const void* H, const void* W_shard, const int64_t* target, int64_t N, int64_t D,
+                                  int64_t V_shard, int64_t vocab_start, int dtype, float* stats3, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected (dtype code %d)", dtype);
+  if (N < 0 || D <= 0 || V_shard <= 0) return set_error(GH_EINVAL, "bad shape");
+  if (D % 8) return set_error(GH_EUNSUPPORTED, "hidden size must be a multiple of 8");
+  if (N == 0) return GH_OK;
+  if (!H || !W_shard || !target || !stats3 || !workspace) return set_error(GH_EINVAL, "null pointer argument");
+  LceLayout L = lce_layout(N, D, V_shard, N, dtype, 0);
+  if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  if (dtype == GH_BF16)
+    return shard_stats_run<__nv_bfloat16>(H, W_shard, target, N, D, V_shard, vocab_start, dtype, stats3, L, ws, st);
+  return shard_stats_run<__half>(H, W_shard, target, N, D, V_shard, vocab_start, dtype, stats3, L, ws, st);
+}
+
+extern "C" int gh_lce_shard_grads(const void* H, const void* W_shard, const int64_t* target, const float* lse,
+                                  int64_t N, int64_t D, int64_t V_shard, int64_t vocab_start, int dtype,
+                                  float z_loss_multiplier, int64_t ignore_index, const float* grad_scale,
+                                  void* grad_input_partial, void* grad_weight_shard, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected (dtype code %d)", dtype);
+  if (N < 0 || D <= 0 || V_shard <= 0) return set_error(GH_EINVAL, "bad shape");
+  if (N == 0) return GH_OK;
+  if (!H || !W_shard || !target || !lse || !workspace) return set_error(GH_EINVAL, "null pointer argument");
+  LceLayout L = lce_layout(N, D, V_shard, N, dtype, 0);
+  if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  if (dtype == GH_BF16)
+    return shard_grads_run<__nv_bfloat16>(H, W_shard, target, lse, N, D, V_shard, vocab_start, dtype,
+                                          z_loss_multiplier, ignore_index, grad_scale, grad_input_partial,
+                                          grad_weight_shard, L, ws, st);
+  return shard_grads_run<__half>(H, W_shard, target, lse, N, D, V_shard, vocab_start, dtype, z_loss_multiplier,
+                                 ignore_index, grad_scale, grad_input_partial, grad_weight_shard, L, ws, st);
 }

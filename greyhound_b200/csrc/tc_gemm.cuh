@@ -57,6 +57,7 @@ struct Params {
   const float* scale;   // optional device scalar multiplying the product
   // EPI_LCE
   const int64_t* labels;  // [M] (chunk rows), compared against the column index
+  int64_t label_offset;   // first vocab id of this GEMM's columns (vocab shards)
   float2* stats;          // [num_n][M] (max, sum-exp) in log2 units
   float* xt;              // [M] target logit (written by the tile holding it)
   int* status;            // device error word (bit 2: pipeline timeout)
@@ -289,7 +290,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       if (EPI == EPI_LCE) {
-        const int64_t lab = row_ok ? p.labels[row] : -1;
+        const int64_t lab = row_ok ? p.labels[row] - p.label_offset : -1;
         const int64_t lab_rel = lab - n0;  // label column inside this tile, if any
         float m_run = kNegInf, s_run = 0.f;
         OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)row * p.ldo;

@@ -137,8 +137,7 @@ class VocabShardedLinearCrossEntropy(torch.autograd.Function):
             scale = torch.ones_like(n)
         else:
             raise ValueError(f"Unsupported reduction: {reduction}")
-        local_t = target - vocab_start
-        stats, logits = lce.vocab_shard_stats(inputs, weight_shard, local_t)
+        stats, state = lce.vocab_shard_stats(inputs, weight_shard, target, vocab_start)
         if world > 1:
             gathered = [torch.empty_like(stats) for _ in range(world)]
             dist.all_gather(gathered, stats, group=group)
@@ -150,7 +149,7 @@ class VocabShardedLinearCrossEntropy(torch.autograd.Function):
         zs = torch.where(valid, lse * lse, torch.zeros_like(lse)).sum()
         loss = (ce + z_loss_multiplier * zs) * scale
         gi, gw = lce.vocab_shard_grads(
-            inputs, weight_shard, logits, local_t, lse, valid, z_loss_multiplier, scale
+            inputs, weight_shard, state, target, vocab_start, lse, z_loss_multiplier, ignore_index, scale
         )
         if world > 1:
             dist.all_reduce(gi, group=group)

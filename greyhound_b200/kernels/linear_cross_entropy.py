@@ -213,55 +213,88 @@ def linear_cross_entropy_loss(
     return ce_sum, z_sum, n_valid
 
 
-def vocab_shard_stats(inputs: Tensor, weight_shard: Tensor, local_target: Tensor) -> tuple[Tensor, Tensor]:
-    """Per-row statistics of one vocab shard: ``[rows, 3]`` fp32 (m, s, target logit).
+def vocab_shard_stats(
+    inputs: Tensor, weight_shard: Tensor, target: Tensor, vocab_start: int
+) -> tuple[Tensor, object]:
+    """Per-row statistics of one vocab shard: ``[rows, 3]`` fp32 ``(lse_shard, 1, x_t)``.
 
-    Returned as ``(lse_local, 1, x_t)`` — an exact (max, sum) pair since
-    ``s * exp(m) = exp(lse_local)`` — with ``x_t = -inf`` when the row's target
-    is not in this shard. Also returns the shard's logits ``[rows, V_local]``
-    (kept for the gradient pass).
+    ``(lse_shard, 1)`` is an exact (max, sum) pair since ``1 * exp(lse) =
+    sum exp(logits)`` over the shard; ``x_t`` is the target logit, ``-inf`` when
+    the row's target is not in this shard. Returns the statistics and an
+    opaque state (the shard's logits) for ``vocab_shard_grads``.
     """
+    from greyhound_b200 import _lib
+
+    rows, D = inputs.shape
+    Vs = weight_shard.shape[0]
+    dev = inputs.device
+    target = target.contiguous()
+    if _tc_ok(inputs, weight_shard.T):
+        x = inputs.contiguous()
+        w = weight_shard.contiguous()
+        lib = _lib.load()
+        code = _lib.dtype_code(inputs.dtype)
+        ws = _lib.workspace(lib.gh_lce_shard_workspace_bytes(rows, D, Vs, code), dev)
+        stats = torch.empty((rows, 3), dtype=torch.float32, device=dev)
+        st = lib.gh_lce_shard_stats(x.data_ptr(), w.data_ptr(), target.data_ptr(), rows, D, Vs, int(vocab_start),
+                                    code, stats.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_of(x))
+        _lib.check(st, "vocab_shard_stats")
+        return stats, ("tc", ws, x, w)
+    # fp32 operands: cuBLAS GEMM + the CE row kernel for the shard logsumexp
     from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad as _ce
 
-    rows = inputs.shape[0]
-    Vl = weight_shard.shape[0]
     logits = inputs @ weight_shard.T
-    lse = torch.empty(rows, dtype=torch.float32, device=inputs.device)
-    never = torch.full_like(local_target, -(1 << 62))
+    lse = torch.empty(rows, dtype=torch.float32, device=dev)
+    never = torch.full_like(target, -(1 << 62))
     _ce(logits, never, 0.0, -(1 << 62), None, lse_out=lse)
-    inside = (local_target >= 0) & (local_target < Vl)
-    xt = logits.gather(1, local_target.clamp(0, Vl - 1)[:, None])[:, 0].float()
+    local = target - vocab_start
+    inside = (local >= 0) & (local < Vs)
+    xt = logits.gather(1, local.clamp(0, Vs - 1)[:, None])[:, 0].float()
     xt = torch.where(inside, xt, torch.full_like(xt, float("-inf")))
-    stats = torch.stack([lse, torch.ones_like(lse), xt], dim=1)
-    return stats, logits
+    return torch.stack([lse, torch.ones_like(lse), xt], dim=1), ("torch", logits)
 
 
 def vocab_shard_grads(
     inputs: Tensor,
     weight_shard: Tensor,
-    logits: Tensor,
-    local_target: Tensor,
+    state: object,
+    target: Tensor,
+    vocab_start: int,
     lse: Tensor,
-    valid: Tensor,
     z_loss_multiplier: float,
+    ignore_index: int,
     scale: Tensor,
 ) -> tuple[Tensor, Tensor]:
     """Gradient pass of one vocab shard given the global per-row logsumexp.
 
-    Writes the shard's logits gradient in place, then returns the partial
-    ``grad_input`` (to be summed over shards) and the shard's ``grad_weight [V_local, D]``.
+    Returns this shard's partial ``grad_input [rows, D]`` (to be summed over
+    shards) and ``grad_weight [V_shard, D]``.
     """
     from greyhound_b200 import _lib
 
-    rows, Vl = logits.shape
-    labels = torch.where(valid, local_target, torch.full_like(local_target, -(1 << 62)))
+    rows, D = inputs.shape
+    Vs = weight_shard.shape[0]
+    dev = inputs.device
+    target = target.contiguous()
+    lse = lse.contiguous().float()
+    sc = scale.reshape(1).float().contiguous()
     lib = _lib.load()
+    if state[0] == "tc":
+        _, ws, x, w = state
+        gi = torch.empty((rows, D), dtype=inputs.dtype, device=dev)
+        gw = torch.empty((Vs, D), dtype=weight_shard.dtype, device=dev)
+        st = lib.gh_lce_shard_grads(x.data_ptr(), w.data_ptr(), target.data_ptr(), lse.data_ptr(), rows, D, Vs,
+                                    int(vocab_start), _lib.dtype_code(inputs.dtype), float(z_loss_multiplier),
+                                    int(ignore_index), sc.data_ptr(), gi.data_ptr(), gw.data_ptr(), ws.data_ptr(),
+                                    ws.numel(), _lib.stream_of(x))
+        _lib.check(st, "vocab_shard_grads")
+        return gi, gw
+    logits = state[1]
+    labels = torch.where(target == ignore_index, torch.full_like(target, -(1 << 62)), target)
     st = lib.gh_logits_grad(
-        logits.data_ptr(), logits.data_ptr(), labels.data_ptr(), lse.contiguous().data_ptr(),
-        rows, Vl, _lib.dtype_code(logits.dtype), float(z_loss_multiplier), -(1 << 62), 0,
-        scale.reshape(1).float().data_ptr(), _lib.stream_of(logits),
+        logits.data_ptr(), logits.data_ptr(), labels.data_ptr(), lse.data_ptr(), rows, Vs,
+        _lib.dtype_code(logits.dtype), float(z_loss_multiplier), -(1 << 62), int(vocab_start),
+        sc.data_ptr(), _lib.stream_of(logits),
     )
     _lib.check(st, "gh_logits_grad")
-    grad_input = logits @ weight_shard
-    grad_weight = (logits.T @ inputs)
-    return grad_input, grad_weight
+    return logits @ weight_shard, logits.T @ inputs

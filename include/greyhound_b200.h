@@ -197,6 +197,30 @@ GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, 
                                 int max_ctas, void* stream);
 
 /* ------------------------------------------------------------------------ *
+ * Vocab-parallel linear cross-entropy (no counterpart in the reference, which
+ * is single-device): this rank holds rows [vocab_start, vocab_start + V_shard)
+ * of W and all N rows of H. Phase 1 computes the shard's logits (kept in the
+ * workspace) with the fused statistics and writes stats3 [N, 3] =
+ * (logsumexp over the shard, 1, target logit or -inf when the target is not
+ * in the shard). The caller all-gathers stats3 over ranks and merges them
+ * into the global per-row logsumexp (exact: lse = M + log sum_p exp(lse_p - M)).
+ * Phase 2 (same workspace) writes the shard's logits gradient with that
+ * global lse, grad_weight_shard [V_shard, D] (row-major) and this shard's
+ * partial grad_input [N, D], which the caller sums over ranks.
+ * ------------------------------------------------------------------------ */
+GH_API size_t gh_lce_shard_workspace_bytes(int64_t N, int64_t D, int64_t V_shard, int dtype);
+GH_API int gh_lce_shard_stats(const void* H, const void* W_shard, const int64_t* target,
+                              int64_t N, int64_t D, int64_t V_shard, int64_t vocab_start,
+                              int dtype, float* stats3, void* workspace, size_t workspace_bytes,
+                              void* stream);
+GH_API int gh_lce_shard_grads(const void* H, const void* W_shard, const int64_t* target,
+                              const float* lse, int64_t N, int64_t D, int64_t V_shard,
+                              int64_t vocab_start, int dtype, float z_loss_multiplier,
+                              int64_t ignore_index, const float* grad_scale,
+                              void* grad_input_partial, void* grad_weight_shard,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Plain tcgen05 GEMM (the GEMMs of the generic chunked_linear_loss path,
  * src/greyhound/ops/chunked_linear_loss.py:82,94,95-101):
  *   out[M, N] = scale * sum_k A[m, k] B[n, k]  (+ addend[M, N])
