@@ -62,7 +62,9 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _i64, _i32, _i32,
          _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
-    "gh_lce_dh_last_chunk": (_i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _vp, _vp, _sz, _i32, _vp]),
+    "gh_lce_dh_last_chunk": (
+        _i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _i64, _i64, _vp, _vp, _sz, _i32, _vp]
+    ),
     "gh_gemm": (
         _i32,
         [_vp, _i64, _i32, _vp, _i64, _i32, _i64, _i64, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _vp, _vp, _vp],

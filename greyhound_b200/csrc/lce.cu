@@ -541,8 +541,9 @@ extern "C" int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* targe
 }
 
 extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype, int64_t chunk_rows,
-                                    int fp32_grad_weight_accum, void* grad_input, void* workspace,
-                                    size_t workspace_bytes, int max_ctas, void* stream) {
+                                    int fp32_grad_weight_accum, int64_t row_begin, int64_t row_end,
+                                    void* grad_input, void* workspace, size_t workspace_bytes, int max_ctas,
+                                    void* stream) {
   if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
   if (N <= 0) return GH_OK;
   LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum);
@@ -551,11 +552,15 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
   const int64_t nchunks = (N + L.chunk - 1) / L.chunk;
   const int64_t s0 = (nchunks - 1) * L.chunk;
   const int64_t rows = N - s0;
-  Operand A{ws + L.logits, L.ldl, 0};
-  Operand B{W, D, 1};
+  if (row_end < 0 || row_end > rows) row_end = rows;
+  if (row_begin < 0) row_begin = 0;
+  if (row_begin >= row_end) return GH_OK;
   const int elt = elt_size(dtype);
-  return run_gemm(dtype, A, B, rows, D, V, static_cast<char*>(grad_input) + s0 * D * elt, dtype, D, nullptr, nullptr,
-                  0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status),
+  Operand A{ws + L.logits + (size_t)row_begin * L.ldl * elt, L.ldl, 0};
+  Operand B{W, D, 1};
+  return run_gemm(dtype, A, B, row_end - row_begin, D, V,
+                  static_cast<char*>(grad_input) + (s0 + row_begin) * D * elt, dtype, D, nullptr, nullptr, 0,
+                  nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status),
                   PROF_GEMM_DH);
 }
 

@@ -103,15 +103,24 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
     _lib.check(st, "linear_cross_entropy")
     if defer:
         work = grad_weight_hook(gw)
-        # leave SMs free for the collective while the deferred dH GEMM runs
+        # The last chunk's dH runs in two parts: the first on fewer SMs, so the
+        # collective's kernels can run beside it, the second on all SMs once the
+        # collective is done (stream-ordered by work.wait()).
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        last_rows = B - ((B - 1) // chunk) * chunk
+        split = min((last_rows // 2 + 255) // 256 * 256, last_rows) if work is not None else last_rows
         st = lib.gh_lce_dh_last_chunk(
-            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), gi.data_ptr(), ws.data_ptr(), ws.numel(),
-            max(1, sms - 20), stream,
+            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, split, gi.data_ptr(), ws.data_ptr(),
+            ws.numel(), max(2, sms - 20) if work is not None else 0, stream,
         )
         _lib.check(st, "linear_cross_entropy dH")
         if work is not None:
             work.wait()
+        st = lib.gh_lce_dh_last_chunk(
+            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), split, -1, gi.data_ptr(), ws.data_ptr(),
+            ws.numel(), 0, stream,
+        )
+        _lib.check(st, "linear_cross_entropy dH")
     elif with_grad and grad_weight_hook is not None:
         w_ = grad_weight_hook(gw)
         if w_ is not None:

@@ -189,10 +189,13 @@ GH_API int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target,
                           void* grad_input, void* grad_weight,
                           float* ce_sum, float* z_sum, float* n_valid,
                           void* workspace, size_t workspace_bytes, void* stream);
-/* grad_input rows of the last chunk, from the dlogits left in the workspace by
- * gh_lce_fwd_bwd(..., GH_LCE_DEFER_LAST_DH). max_ctas <= 0: all SMs. */
+/* grad_input rows [row_begin, row_end) of the last chunk (offsets inside the
+ * chunk; row_end < 0: to the end), from the dlogits left in the workspace by
+ * gh_lce_fwd_bwd(..., GH_LCE_DEFER_LAST_DH). max_ctas <= 0: all SMs; fewer
+ * leave SMs to a concurrently running collective. */
 GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype,
                                 int64_t chunk_rows, int fp32_grad_weight_accum,
+                                int64_t row_begin, int64_t row_end,
                                 void* grad_input, void* workspace, size_t workspace_bytes,
                                 int max_ctas, void* stream);
 
