@@ -72,12 +72,12 @@ def _patch():
     D.scale_by = lambda t, g: t * g
 
 
-def _init(rank, world, port):
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
+def _init(rank, world, store_path):
+    # file rendezvous: no TCP port to race for between concurrently started tests
     import datetime
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    dist.init_process_group("gloo", init_method=f"file://{store_path}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
 
 
 def row_sharded_worker(rank, world, port, data, out_q):

@@ -4,7 +4,8 @@ Kernels are replaced by CPU stand-ins (tests/_dist_workers.py); the
 communication code of greyhound_b200.distributed runs for real. Results are
 compared with a single-process computation on the full data."""
 
-import socket
+import os
+import tempfile
 
 import pytest
 import torch
@@ -13,19 +14,13 @@ import torch.multiprocessing as mp
 import _dist_workers as W
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
-
-
 def _run(worker, data, world=2, timeout=120):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=worker, args=(r, world, port, data, q)) for r in range(world)]
+    fd, store = tempfile.mkstemp(prefix="gh_gloo_")
+    os.close(fd)
+    os.unlink(store)
+    procs = [ctx.Process(target=worker, args=(r, world, store, data, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=timeout) for _ in range(world)]
