@@ -101,6 +101,46 @@ __device__ __forceinline__ uint4 ld16_last(const void* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
   return v;
 }
+// 32-byte (256-bit) accesses, sm_100: half the memory instructions of 16-byte ones.
+struct U8 {
+  uint32_t w[8];
+};
+__device__ __forceinline__ U8 ld32(const void* p) {
+  U8 v;
+  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                 "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ U8 ld32_last(const void* p) {
+  U8 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                 "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void st32(void* p, const U8& v) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
+               "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+               : "memory");
+}
+template <typename T>
+struct Vec32 {
+  static constexpr int N = 32 / sizeof(T);
+  U8 raw;
+  __device__ __forceinline__ void to_float(float (&f)[N]) const {
+    const T* p = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) f[i] = Elt<T>::to_f(p[i]);
+  }
+  __device__ __forceinline__ void from_float(const float (&f)[N]) {
+    T* p = reinterpret_cast<T*>(&raw);
+#pragma unroll
+    for (int i = 0; i < N; ++i) p[i] = Elt<T>::from_f(f[i]);
+  }
+};
 __device__ __forceinline__ void st16(void* p, uint4 v) {
   asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};"
                :: "l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
@@ -147,6 +187,20 @@ __device__ __forceinline__ MS ms_fold(MS a, const float (&t)[N]) {
   float s = a.s * fast_exp2(a.m - m);
 #pragma unroll
   for (int i = 0; i < N; ++i) s += fast_exp2(t[i] - m);
+  return {m, s};
+}
+// Same for raw (unscaled) values x[i]: the max is taken on x and the scale
+// folded into one FFMA per element, exp2(x * log2e - m).
+template <int N>
+__device__ __forceinline__ MS ms_fold_raw(MS a, const float (&x)[N]) {
+  float bm = x[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i) bm = fmaxf(bm, x[i]);
+  const float m = fmaxf(a.m, bm * kLog2e);
+  if (m == kNegInf) return a;
+  float s = a.s * fast_exp2(a.m - m);
+#pragma unroll
+  for (int i = 0; i < N; ++i) s += fast_exp2(fmaf(x[i], kLog2e, -m));
   return {m, s};
 }
 __device__ __forceinline__ MS ms_fold1(MS a, float t) {
@@ -205,13 +259,13 @@ struct RowSplit {
   int64_t nvec;   // number of 16-byte vectors
   int64_t tail0;  // first element of the scalar tail
 };
-__device__ __forceinline__ RowSplit row_split(uintptr_t addr, int64_t n, int elt) {
+__device__ __forceinline__ RowSplit row_split(uintptr_t addr, int64_t n, int elt, int vbytes = 16) {
   RowSplit r;
-  int64_t mis = (int64_t)(addr & 15);
-  int64_t head = mis == 0 ? 0 : (16 - mis) / elt;
+  int64_t mis = (int64_t)(addr & (vbytes - 1));
+  int64_t head = mis == 0 ? 0 : (vbytes - mis) / elt;
   if (head > n) head = n;
   r.head = head;
-  const int per = 16 / elt;
+  const int per = vbytes / elt;
   r.nvec = (n - head) / per;
   r.tail0 = head + r.nvec * per;
   return r;

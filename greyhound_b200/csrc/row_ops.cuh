@@ -9,43 +9,41 @@
 namespace gh {
 namespace {
 
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 2;  // x 32-byte vectors in flight per thread
 
 // This thread's (max, sum) partial over x[0, n), in log2 units.
 template <typename T, int THREADS, int UNROLL>
 __device__ __forceinline__ MS row_partial(const T* __restrict__ x, int64_t n) {
-  constexpr int PER = 16 / sizeof(T);
-  const RowSplit sp = row_split(reinterpret_cast<uintptr_t>(x), n, sizeof(T));
+  constexpr int PER = 32 / sizeof(T);
+  const RowSplit sp = row_split(reinterpret_cast<uintptr_t>(x), n, sizeof(T), 32);
   MS acc = ms_empty();
   const int tid = threadIdx.x;
   for (int64_t i = tid; i < sp.head; i += THREADS)
     acc = ms_fold1(acc, Elt<T>::to_f(x[i]) * kLog2e);
   for (int64_t i = sp.tail0 + tid; i < n; i += THREADS)
     acc = ms_fold1(acc, Elt<T>::to_f(x[i]) * kLog2e);
-  const uint4* xv = reinterpret_cast<const uint4*>(x + sp.head);
+  const U8* xv = reinterpret_cast<const U8*>(x + sp.head);
   int64_t i = tid;
   for (; i + (int64_t)(UNROLL - 1) * THREADS < sp.nvec; i += (int64_t)UNROLL * THREADS) {
-    Vec16<T> r[UNROLL];
+    Vec32<T> r[UNROLL];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld16(xv + i + u * THREADS);
+    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld32(xv + i + u * THREADS);
     float t[UNROLL * PER];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       float f[PER];
       r[u].to_float(f);
 #pragma unroll
-      for (int k = 0; k < PER; ++k) t[u * PER + k] = f[k] * kLog2e;
+      for (int k = 0; k < PER; ++k) t[u * PER + k] = f[k];
     }
-    acc = ms_fold<UNROLL * PER>(acc, t);
+    acc = ms_fold_raw<UNROLL * PER>(acc, t);
   }
   for (; i < sp.nvec; i += THREADS) {
-    Vec16<T> r;
-    r.raw = ld16(xv + i);
+    Vec32<T> r;
+    r.raw = ld32(xv + i);
     float f[PER];
     r.to_float(f);
-#pragma unroll
-    for (int k = 0; k < PER; ++k) f[k] *= kLog2e;
-    acc = ms_fold<PER>(acc, f);
+    acc = ms_fold_raw<PER>(acc, f);
   }
   return acc;
 }
@@ -55,8 +53,8 @@ __device__ __forceinline__ MS row_partial(const T* __restrict__ x, int64_t n) {
 template <typename T, int THREADS, int UNROLL>
 __device__ __forceinline__ void row_grad(const T* x, T* y, int64_t n, int64_t lab,
                                          float mm, float coef, float sub) {
-  constexpr int PER = 16 / sizeof(T);
-  const RowSplit sp = row_split(reinterpret_cast<uintptr_t>(x), n, sizeof(T));
+  constexpr int PER = 32 / sizeof(T);
+  const RowSplit sp = row_split(reinterpret_cast<uintptr_t>(x), n, sizeof(T), 32);
   const int tid = threadIdx.x;
   auto scalar = [&](int64_t c) {
     float g = fast_exp2(Elt<T>::to_f(x[c]) * kLog2e - mm) * coef;
@@ -65,43 +63,48 @@ __device__ __forceinline__ void row_grad(const T* x, T* y, int64_t n, int64_t la
   };
   for (int64_t c = tid; c < sp.head; c += THREADS) scalar(c);
   for (int64_t c = sp.tail0 + tid; c < n; c += THREADS) scalar(c);
-  const uint4* xv = reinterpret_cast<const uint4*>(x + sp.head);
-  uint4* yv = reinterpret_cast<uint4*>(y + sp.head);
+  const U8* xv = reinterpret_cast<const U8*>(x + sp.head);
+  U8* yv = reinterpret_cast<U8*>(y + sp.head);
   const int64_t lab_rel = lab - sp.head;  // label position relative to the vector run
+  // vector holding the label (or -1): one compare per vector, not per element
+  const int64_t lab_vec = (lab_rel >= 0 && lab_rel < sp.nvec * PER) ? lab_rel / PER : -1;
+  const int lab_k = (int)(lab_rel - (lab_vec < 0 ? 0 : lab_vec) * PER);
   int64_t i = tid;
   for (; i + (int64_t)(UNROLL - 1) * THREADS < sp.nvec; i += (int64_t)UNROLL * THREADS) {
-    Vec16<T> r[UNROLL];
+    Vec32<T> r[UNROLL];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld16_last(xv + i + u * THREADS);
+    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld32_last(xv + i + u * THREADS);
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       float f[PER];
       r[u].to_float(f);
-      const int64_t base = (i + u * THREADS) * PER;
 #pragma unroll
-      for (int k = 0; k < PER; ++k) {
-        f[k] = fast_exp2(f[k] * kLog2e - mm) * coef;
-        if (base + k == lab_rel) f[k] -= sub;
+      for (int k = 0; k < PER; ++k) f[k] = fast_exp2(fmaf(f[k], kLog2e, -mm)) * coef;
+      if (i + u * THREADS == lab_vec) {
+#pragma unroll
+        for (int k = 0; k < PER; ++k)
+          if (k == lab_k) f[k] -= sub;
       }
-      Vec16<T> o;
+      Vec32<T> o;
       o.from_float(f);
-      st16(yv + i + u * THREADS, o.raw);
+      st32(yv + i + u * THREADS, o.raw);
     }
   }
   for (; i < sp.nvec; i += THREADS) {
-    Vec16<T> r;
-    r.raw = ld16_last(xv + i);
+    Vec32<T> r;
+    r.raw = ld32_last(xv + i);
     float f[PER];
     r.to_float(f);
-    const int64_t base = i * PER;
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-      f[k] = fast_exp2(f[k] * kLog2e - mm) * coef;
-      if (base + k == lab_rel) f[k] -= sub;
+    for (int k = 0; k < PER; ++k) f[k] = fast_exp2(fmaf(f[k], kLog2e, -mm)) * coef;
+    if (i == lab_vec) {
+#pragma unroll
+      for (int k = 0; k < PER; ++k)
+        if (k == lab_k) f[k] -= sub;
     }
-    Vec16<T> o;
+    Vec32<T> o;
     o.from_float(f);
-    st16(yv + i, o.raw);
+    st32(yv + i, o.raw);
   }
 }
 
