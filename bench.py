@@ -250,23 +250,52 @@ def bench_lce(args, rank, world, local):
     launches = (_lib.launch_count() - c0) // (args.steps + args.warmup)
     clocks = clk.summary()
 
-    # end-to-end: H/targets copied from pinned host memory every step, loss read back
+    # end-to-end: each step's H/targets copied from pinned host memory and its
+    # loss read back. The copy of step k+1's inputs is issued on a copy stream
+    # while step k computes (double-buffered, as a training input pipeline
+    # does); the first timed step copies its own inputs inside the timed region.
     H_host = H.detach().cpu().pin_memory()
     t_host = t.cpu().pin_memory()
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
-    Hd = torch.empty_like(H.detach())
-    td = torch.empty_like(t)
+    bufs = [(torch.empty_like(H.detach()), torch.empty_like(t)) for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device=dev)
+    state = {"k": 0, "ready": None, "done": [None, None]}
+
+    def issue(k):
+        Hb, tb = bufs[k % 2]
+        prev = state["done"][k % 2]
+        with torch.cuda.stream(copy_stream):
+            if prev is not None:
+                copy_stream.wait_event(prev)  # the step that last used this buffer is finished
+            Hb.copy_(H_host, non_blocking=True)
+            tb.copy_(t_host, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy_stream)
+        return ev
 
     def e2e_step():
-        Hd.copy_(H_host, non_blocking=True)
-        td.copy_(t_host, non_blocking=True)
-        Hin = Hd.detach().requires_grad_(True)
+        k = state["k"]
+        ev = state["ready"] if state["ready"] is not None else issue(k)
+        torch.cuda.current_stream().wait_event(ev)
+        state["ready"] = issue(k + 1)
+        Hb, tb = bufs[k % 2]
+        Hin = Hb.detach().requires_grad_(True)
         W.grad = None
-        loss = fn(Hin, W, td)
+        loss = fn(Hin, W, tb)
         loss.backward()
         loss_host.copy_(loss.detach(), non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        state["done"][k % 2] = done
+        state["k"] = k + 1
 
-    ms_e2e = time_steps(e2e_step, args.steps, args.warmup, world)
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    state["ready"] = None  # the first timed step copies its own inputs
+    ms_e2e = time_steps(e2e_step, args.steps, 0, world)
+    # the last prefetch belongs to a step outside the timed region
+    torch.cuda.synchronize()
 
     peaks, peak_src = load_peaks()
     flops = 6.0 * N * D * V
@@ -331,6 +360,7 @@ def bench_lce(args, rank, world, local):
             "ms_per_step": ms_e2e,
             "h2d_bytes_per_step": H.numel() * 2 + t.numel() * 8,
             "d2h_bytes_per_step": 4,
+            "input_pipeline": "pinned host -> device copy of every step's inputs, issued one step ahead on a copy stream",
         },
         "gpu_launches": launches * args.steps,
         "gpu_launches_per_step": launches,

@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "gh_sls_bwd": (_i32, [_vp, _vp, _i32, _vp, _vp, _i32, _i64, _i64, _i32, _vp, _vp]),
     "gh_logits_grad": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _f32, _i64, _i64, _vp, _vp]),
     "gh_lce_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i32, _i32]),
+    "gh_lce_loss_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i32]),
     "gh_lce_fwd_bwd": (
         _i32,
         [_vp, _vp, _vp, _i64, _i64, _i64, _i32, _f32, _i64, _i32, _vp, _i64, _i32, _i32,

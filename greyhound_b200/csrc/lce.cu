@@ -299,7 +299,8 @@ struct LceLayout {
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
-LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, int fp32_accum) {
+LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, int fp32_accum,
+                     bool loss_only = false) {
   LceLayout L;
   if (chunk <= 0 || chunk > N) chunk = N;
   L.chunk = chunk;
@@ -307,14 +308,15 @@ LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, 
   L.num_n = (int)((V + BN - 1) / BN);
   const int elt = elt_size(dtype);
   size_t off = 256;
-  L.logits = off; off = al256(off + (size_t)chunk * L.ldl * elt);
+  L.logits = off;
+  if (!loss_only) off = al256(off + (size_t)chunk * L.ldl * elt);
   L.stats = off;  off = al256(off + sizeof(float2) * (size_t)L.num_n * chunk);
   L.xt = off;     off = al256(off + sizeof(float) * chunk);
   L.lse = off;    off = al256(off + sizeof(float) * chunk);
   L.row_ce = off; off = al256(off + sizeof(float) * N);
   L.row_z = off;  off = al256(off + sizeof(float) * N);
   const int64_t nchunks = N > 0 ? (N + chunk - 1) / chunk : 0;
-  L.need_acc = fp32_accum && nchunks > 1;
+  L.need_acc = !loss_only && fp32_accum && nchunks > 1;
   L.acc = off;
   if (L.need_acc) off = al256(off + sizeof(float) * (size_t)D * V);
   L.total = off;
@@ -383,7 +385,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       gemm::Params p{};
       set_tiles(p, rows, V, D, pair);
       p.raster = 0;  // m fastest: concurrent CTAs share one W band, H stays in L2
-      p.out = logits;
+      p.out = with_grad ? logits : nullptr;  // forward only: statistics, no logits
       p.ldo = L.ldl;
       p.vec_ok = ((L.ldl * (int64_t)sizeof(T)) & 15) == 0;
       p.labels = tc;
@@ -511,6 +513,11 @@ extern "C" size_t gh_lce_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_
   return lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum).total;
 }
 
+extern "C" size_t gh_lce_loss_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows, int dtype) {
+  if (N < 0 || D <= 0 || V <= 0 || elt_size(dtype) != 2) return 0;
+  return lce_layout(N, D, V, chunk_rows, dtype, 0, true).total;
+}
+
 extern "C" int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target, int64_t N, int64_t D, int64_t V,
                               int dtype, float z_loss_multiplier, int64_t ignore_index, int mean_reduction,
                               const float* grad_scale, int64_t chunk_rows, int fp32_grad_weight_accum, int flags,
@@ -523,7 +530,8 @@ extern "C" int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* targe
   if (D % 8) return set_error(GH_EUNSUPPORTED, "hidden size must be a multiple of 8 (got %lld)", (long long)D);
   if (!H || !W || !target || !ce_sum || !z_sum || !n_valid || !workspace)
     return set_error(GH_EINVAL, "null pointer argument");
-  LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum);
+  const bool loss_only = !grad_input && !grad_weight;
+  LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum, loss_only);
   if (workspace_bytes < L.total)
     return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
   cudaStream_t st = static_cast<cudaStream_t>(stream);

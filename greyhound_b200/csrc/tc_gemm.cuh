@@ -55,7 +55,7 @@ struct Params {
   const void* add_same; // optional addend in the output type [M, ldadd]
   int64_t ldadd;
   const float* scale;   // optional device scalar multiplying the product
-  // EPI_LCE
+  // EPI_LCE (out == nullptr: statistics only, no logits written)
   const int64_t* labels;  // [M] (chunk rows), compared against the column index
   int64_t label_offset;   // first vocab id of this GEMM's columns (vocab shards)
   float2* stats;          // [num_n][M] (max, sum-exp) in log2 units
@@ -319,7 +319,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (col0 + j < p.N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
           s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
           m_run = mnew;
-          if (row_ok) store_row32<OutT>(orow, col0, p.N, x, p.vec_ok);
+          if (row_ok && p.out) store_row32<OutT>(orow, col0, p.N, x, p.vec_ok);
         }
         if (row_ok) p.stats[(int64_t)nt * p.M + row] = make_float2(m_run, s_run);
       } else {

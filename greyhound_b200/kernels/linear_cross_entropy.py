@@ -89,7 +89,11 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
     chunk = chunk_size_for(B, D, V, inputs.element_size())
     lib = _lib.load()
     code = _lib.dtype_code(inputs.dtype)
-    ws = _lib.workspace(lib.gh_lce_workspace_bytes(B, D, V, chunk, code, int(fp32_accum)), dev)
+    if with_grad:
+        ws_bytes = lib.gh_lce_workspace_bytes(B, D, V, chunk, code, int(fp32_accum))
+    else:  # statistics only: the logits never touch memory
+        ws_bytes = lib.gh_lce_loss_workspace_bytes(B, D, V, chunk, code)
+    ws = _lib.workspace(ws_bytes, dev)
     ce_sum = torch.empty((), dtype=torch.float32, device=dev)
     z_sum = torch.empty((), dtype=torch.float32, device=dev)
     n_valid = torch.empty((), dtype=torch.float32, device=dev)

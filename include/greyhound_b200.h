@@ -181,6 +181,11 @@ enum { GH_LCE_DEFER_LAST_DH = 1 };
 
 GH_API size_t gh_lce_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows,
                                      int dtype, int fp32_grad_weight_accum);
+/* Workspace for the loss-only form (grad_input == grad_weight == NULL): the
+ * forward-only path (src/greyhound/ops/chunked_linear_cross_entropy.py:91-132)
+ * keeps only per-row statistics, the logits are never written to memory. */
+GH_API size_t gh_lce_loss_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows,
+                                          int dtype);
 GH_API int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target,
                           int64_t N, int64_t D, int64_t V, int dtype,
                           float z_loss_multiplier, int64_t ignore_index,
