@@ -113,6 +113,15 @@ __device__ __forceinline__ U8 ld32(const void* p) {
                : "l"(p));
   return v;
 }
+// First read of a row that will be read again soon: keep it in L2.
+__device__ __forceinline__ U8 ld32_keep(const void* p) {
+  U8 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::evict_last.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                 "=r"(v.w[6]), "=r"(v.w[7])
+               : "l"(p));
+  return v;
+}
 __device__ __forceinline__ U8 ld32_last(const void* p) {
   U8 v;
   asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -124,6 +133,14 @@ __device__ __forceinline__ U8 ld32_last(const void* p) {
 __device__ __forceinline__ void st32(void* p, const U8& v) {
   asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.w[0]), "r"(v.w[1]),
                "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]), "r"(v.w[7])
+               : "memory");
+}
+// Store that must not displace lines still waiting to be re-read (the
+// gradient written by a row kernel whose input row is re-read from L2).
+__device__ __forceinline__ void st32_stream(void* p, const U8& v) {
+  asm volatile("st.global.L1::no_allocate.L2::evict_first.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p),
+               "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]), "r"(v.w[6]),
+               "r"(v.w[7])
                : "memory");
 }
 template <typename T>

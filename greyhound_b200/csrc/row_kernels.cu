@@ -49,7 +49,7 @@ ce_fused_kernel(const T* __restrict__ logits, T* dlogits, const int64_t* __restr
     // in-place gradient other threads overwrite it right after.
     float x_lab = 0.f;
     if (threadIdx.x == 0 && valid) x_lab = Elt<T>::to_f(x[lab]);
-    MS tot = block_merge<THREADS>(row_partial<T, THREADS, UNROLL>(x, V), scratch);
+    MS tot = block_merge<THREADS>(row_partial<T, THREADS, UNROLL, true>(x, V), scratch);
     const float lse2 = tot.m + fast_log2(tot.s);
     const float lse = lse2 * kLn2;
     if (threadIdx.x == 0) {

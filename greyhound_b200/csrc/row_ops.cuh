@@ -12,7 +12,9 @@ namespace {
 constexpr int kUnroll = 2;  // x 32-byte vectors in flight per thread
 
 // This thread's (max, sum) partial over x[0, n), in log2 units.
-template <typename T, int THREADS, int UNROLL>
+// KEEP: the row is read again right after (CE): first-read loads marked
+// evict_last so the re-read hits L2.
+template <typename T, int THREADS, int UNROLL, bool KEEP = false>
 __device__ __forceinline__ MS row_partial(const T* __restrict__ x, int64_t n) {
   constexpr int PER = 32 / sizeof(T);
   const RowSplit sp = row_split(reinterpret_cast<uintptr_t>(x), n, sizeof(T), 32);
@@ -27,7 +29,7 @@ __device__ __forceinline__ MS row_partial(const T* __restrict__ x, int64_t n) {
   for (; i + (int64_t)(UNROLL - 1) * THREADS < sp.nvec; i += (int64_t)UNROLL * THREADS) {
     Vec32<T> r[UNROLL];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld32(xv + i + u * THREADS);
+    for (int u = 0; u < UNROLL; ++u) r[u].raw = KEEP ? ld32_keep(xv + i + u * THREADS) : ld32(xv + i + u * THREADS);
     float t[UNROLL * PER];
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
@@ -40,7 +42,7 @@ __device__ __forceinline__ MS row_partial(const T* __restrict__ x, int64_t n) {
   }
   for (; i < sp.nvec; i += THREADS) {
     Vec32<T> r;
-    r.raw = ld32(xv + i);
+    r.raw = KEEP ? ld32_keep(xv + i) : ld32(xv + i);
     float f[PER];
     r.to_float(f);
     acc = ms_fold_raw<PER>(acc, f);
@@ -87,7 +89,7 @@ __device__ __forceinline__ void row_grad(const T* x, T* y, int64_t n, int64_t la
       }
       Vec32<T> o;
       o.from_float(f);
-      st32(yv + i + u * THREADS, o.raw);
+      st32_stream(yv + i + u * THREADS, o.raw);
     }
   }
   for (; i < sp.nvec; i += THREADS) {
@@ -104,7 +106,7 @@ __device__ __forceinline__ void row_grad(const T* x, T* y, int64_t n, int64_t la
     }
     Vec32<T> o;
     o.from_float(f);
-    st32(yv + i, o.raw);
+    st32_stream(yv + i, o.raw);
   }
 }
 
