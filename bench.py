@@ -425,13 +425,24 @@ def bench_rows(args, rank, world, local, which):
         step = lambda: cross_entropy_with_grad(x, t, 0.0, -100, out, mean_reduction=True)  # noqa: E731
         nbytes = 2 * rows * V * 2 + rows * 8
         metric = f"cross_entropy fwd+grad GB/s [{rows},{V}] bf16"
-    else:
+    elif which == "sls":
         rows, V = args.rows or 65536, args.vocab or 151936
         x = (torch.randn(rows, V, device=dev, generator=g) * 3).to(torch.bfloat16)
         t = torch.randint(0, V, (rows,), device=dev, generator=g)
         step = lambda: selective_log_softmax_with_lse(x, t, out_dtype=torch.float32)  # noqa: E731
         nbytes = rows * V * 2 + rows * 8 + rows * 4
         metric = f"selective_log_softmax fwd GB/s [{rows},{V}] bf16"
+    else:  # sls_bwd: grad_logits = g * (onehot - softmax), from the saved lse
+        from greyhound_b200.kernels.logprobs import selective_log_softmax_backward_kernel
+
+        rows, V = args.rows or 65536, args.vocab or 151936
+        x = (torch.randn(rows, V, device=dev, generator=g) * 3).to(torch.bfloat16)
+        t = torch.randint(0, V, (rows,), device=dev, generator=g)
+        _, lse = selective_log_softmax_with_lse(x, t, out_dtype=torch.float32)
+        go = torch.randn(rows, device=dev, generator=g)
+        step = lambda: selective_log_softmax_backward_kernel(x, t, lse, go)  # noqa: E731
+        nbytes = 2 * rows * V * 2 + rows * (8 + 4 + 4)
+        metric = f"selective_log_softmax bwd GB/s [{rows},{V}] bf16"
     c0 = _lib.launch_count()
     with ClockSampler(local) as clk:
         ms = time_steps(step, args.steps, args.warmup, world)
@@ -455,7 +466,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["lce", "ce", "sls"], default="lce")
+    ap.add_argument("--workload", choices=["lce", "ce", "sls", "sls_bwd"], default="lce")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-step-seconds", type=float, default=8.0)
     # shape overrides, only for small profiler captures (the default is the workload)
