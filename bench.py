@@ -373,6 +373,82 @@ def bench_lce(args, rank, world, local):
     return line
 
 
+def bench_lce70b(args, rank, world, local):
+    """Llama-3-70B-scale head, H[65536, 8192], W[128256, 8192]
+    ~N(0, 0.015), 2% ignore, mean. ``--parallel rows``: the 65536 rows split over
+    the ranks, W replicated, dW all-reduced; ``--parallel vocab``: W split by
+    vocabulary rows, H replicated, per-row statistics all-gathered and the
+    partial dH all-reduced. Total work fixed: strong scaling."""
+    from greyhound_b200 import _lib
+    from greyhound_b200.distributed import (
+        row_sharded_linear_cross_entropy,
+        shard_range,
+        vocab_sharded_linear_cross_entropy,
+    )
+    from greyhound_b200.nn.functional import chunked_linear_cross_entropy
+
+    N, D, V = args.rows or 65536, args.hidden or 8192, args.vocab or 128256
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev)
+    if args.parallel == "vocab" and world > 1:
+        g.manual_seed(4)  # identical H / targets on every rank
+        H = torch.randn(N, D, device=dev, generator=g).to(torch.bfloat16)
+        t = torch.randint(0, V, (N,), device=dev, generator=g)
+        t[torch.rand(N, device=dev, generator=g) < 0.02] = -100
+        vs, ve = shard_range(V, rank, world)
+        g.manual_seed(1000 + rank)
+        W = (torch.randn(ve - vs, D, device=dev, generator=g) * 0.015).to(torch.bfloat16)
+        fn = lambda h, w, tt: vocab_sharded_linear_cross_entropy(h, w, tt, vs)  # noqa: E731
+        par = f"vocab-parallel x{world} (stats all-gather + dH all-reduce)"
+    else:
+        rs, re_ = shard_range(N, rank, world)
+        g.manual_seed(4 + rank)
+        H = torch.randn(re_ - rs, D, device=dev, generator=g).to(torch.bfloat16)
+        t = torch.randint(0, V, (re_ - rs,), device=dev, generator=g)
+        t[torch.rand(re_ - rs, device=dev, generator=g) < 0.02] = -100
+        g.manual_seed(1000)
+        W = (torch.randn(V, D, device=dev, generator=g) * 0.015).to(torch.bfloat16)
+        fn = row_sharded_linear_cross_entropy if world > 1 else chunked_linear_cross_entropy
+        par = f"row-sharded x{world} (dW all-reduce)" if world > 1 else "single GPU"
+    H.requires_grad_(True)
+    W.requires_grad_(True)
+
+    def step():
+        H.grad = None
+        W.grad = None
+        fn(H, W, t).backward()
+
+    c0 = _lib.launch_count()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    _lib.profile_read(reset=True)
+    _lib.profile_enable(True)
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, 0, world)
+    _lib.profile_enable(False)
+    prof = _lib.profile_read(reset=True)
+    launches = (_lib.launch_count() - c0) // (args.steps + args.warmup)
+    peaks, src = load_peaks()
+    tflops_gpu = 6.0 * N * D * V / world / (ms * 1e-3) / 1e12
+    kernels = {c: {"launches_per_step": n / args.steps, "ms_per_step": tot / args.steps}
+               for c, (tot, n) in prof.items() if n}
+    return {
+        "metric": "linear-CE fwd+bwd tokens/s, Llama-3-70B-scale head", "value": N / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded randn of the workload's shapes)",
+        "config": {"workload": "Llama-3-70B-scale head chunked_linear_cross_entropy fwd+bwd (BASELINE configs[4])",
+                   "N": N, "D": D, "V": V, "parallelism": par, "l2": "inputs larger than L2"},
+        "tflops_per_gpu": tflops_gpu,
+        "roofline": {"bound": "tensor", "kernel": "whole step (6*N*D*V / GPUs)", "achieved": tflops_gpu,
+                     "peak": peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "unit": "TFLOP/s",
+                     "frac": tflops_gpu / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
+                     "peak_source": src, "traffic": None},
+        "kernels": kernels, "gpu_launches": launches * args.steps, "clocks": clk.summary(),
+    }
+
+
 def bench_reference(args, rank, world):
     """CPU restatement of the reference (the oracle) on the host cores."""
     if rank != 0:
@@ -466,7 +542,8 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["lce", "ce", "sls", "sls_bwd"], default="lce")
+    ap.add_argument("--workload", choices=["lce", "lce70b", "ce", "sls", "sls_bwd"], default="lce")
+    ap.add_argument("--parallel", choices=["rows", "vocab"], default="rows", help="lce70b sharding mode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-step-seconds", type=float, default=8.0)
     # shape overrides, only for small profiler captures (the default is the workload)
@@ -486,6 +563,8 @@ def main() -> int:
     rank, world, local = dist_setup(args.gpus)
     if args.workload == "lce":
         line = bench_lce(args, rank, world, local)
+    elif args.workload == "lce70b":
+        line = bench_lce70b(args, rank, world, local)
     else:
         line = bench_rows(args, rank, world, local, args.workload)
     if rank == 0:
