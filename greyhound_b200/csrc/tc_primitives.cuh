@@ -39,6 +39,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the waiting thread sleeps in hardware
+// (woken when the phase completes or after about `ns`) instead of spinning,
+// which saves issue slots and power in the persistent GEMM's idle roles.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -54,8 +68,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if ((++n & 255u) == 0) {
+  while (!mbar_try_wait_sleep(bar, parity, 20000)) {
+    if ((++n & 15u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > limit_ns) {
         *abort = 1;
