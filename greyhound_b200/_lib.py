@@ -73,6 +73,7 @@ SIGNATURES: dict[str, tuple] = {
     "gh_scale": (_i32, [_vp, _vp, _i64, _i32, _vp, _vp]),
     "gh_lce_shard_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
     "gh_lce_shard_stats": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _sz, _vp]),
+    "gh_lce_shard_dw": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _sz, _i32, _vp]),
     "gh_lce_shard_grads": (
         _i32,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp],

@@ -628,3 +628,18 @@ extern "C" int gh_lce_shard_grads(const void* H, const void* W_shard, const int6
   return shard_grads_run<__half>(H, W_shard, target, lse, N, D, V_shard, vocab_start, dtype, z_loss_multiplier,
                                  ignore_index, grad_scale, grad_input_partial, grad_weight_shard, L, ws, st);
 }
+
+extern "C" int gh_lce_shard_dw(const void* H, int64_t N, int64_t D, int64_t V_shard, int dtype,
+                               void* grad_weight_shard, void* workspace, size_t workspace_bytes, int max_ctas,
+                               void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected (dtype code %d)", dtype);
+  if (N < 0 || D <= 0 || V_shard <= 0) return set_error(GH_EINVAL, "bad shape");
+  if (N == 0) return GH_OK;
+  if (!H || !grad_weight_shard || !workspace) return set_error(GH_EINVAL, "null pointer argument");
+  LceLayout L = lce_layout(N, D, V_shard, N, dtype, 0);
+  if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
+  char* ws = static_cast<char*>(workspace);
+  return run_gemm(dtype, Operand{ws + L.logits, L.ldl, 1}, Operand{H, D, 1}, V_shard, D, N, grad_weight_shard, dtype,
+                  D, nullptr, nullptr, 0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream),
+                  reinterpret_cast<int*>(ws + L.status), PROF_GEMM_DW);
+}

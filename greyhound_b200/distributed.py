@@ -148,11 +148,14 @@ class VocabShardedLinearCrossEntropy(torch.autograd.Function):
         ce = torch.where(valid, lse - x_t, torch.zeros_like(lse)).sum()
         zs = torch.where(valid, lse * lse, torch.zeros_like(lse)).sum()
         loss = (ce + z_loss_multiplier * zs) * scale
-        gi, gw = lce.vocab_shard_grads(
-            inputs, weight_shard, state, target, vocab_start, lse, z_loss_multiplier, ignore_index, scale
-        )
+        hook = None
         if world > 1:
-            dist.all_reduce(gi, group=group)
+            def hook(gi_partial: Tensor):
+                return dist.all_reduce(gi_partial, group=group, async_op=True)
+        gi, gw = lce.vocab_shard_grads(
+            inputs, weight_shard, state, target, vocab_start, lse, z_loss_multiplier, ignore_index, scale,
+            grad_input_hook=hook,
+        )
         ctx.save_for_backward(gi, gw)
         return loss
 

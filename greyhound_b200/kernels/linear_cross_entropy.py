@@ -291,11 +291,15 @@ def vocab_shard_grads(
     z_loss_multiplier: float,
     ignore_index: int,
     scale: Tensor,
+    grad_input_hook=None,
 ) -> tuple[Tensor, Tensor]:
     """Gradient pass of one vocab shard given the global per-row logsumexp.
 
-    Returns this shard's partial ``grad_input [rows, D]`` (to be summed over
-    shards) and ``grad_weight [V_shard, D]``.
+    Returns this shard's partial ``grad_input [rows, D]`` and ``grad_weight
+    [V_shard, D]``. ``grad_input_hook(grad_input)`` (the cross-shard sum,
+    returning an async work handle or None) is called as soon as the partial
+    grad_input exists; the dW GEMM runs while it is in flight and the handle
+    is waited on before returning.
     """
     from greyhound_b200 import _lib
 
@@ -310,11 +314,22 @@ def vocab_shard_grads(
         _, ws, x, w = state
         gi = torch.empty((rows, D), dtype=inputs.dtype, device=dev)
         gw = torch.empty((Vs, D), dtype=weight_shard.dtype, device=dev)
+        stream = _lib.stream_of(x)
+        # dlogits + partial dH first, so the dH all-reduce can overlap the dW GEMM
         st = lib.gh_lce_shard_grads(x.data_ptr(), w.data_ptr(), target.data_ptr(), lse.data_ptr(), rows, D, Vs,
                                     int(vocab_start), _lib.dtype_code(inputs.dtype), float(z_loss_multiplier),
-                                    int(ignore_index), sc.data_ptr(), gi.data_ptr(), gw.data_ptr(), ws.data_ptr(),
-                                    ws.numel(), _lib.stream_of(x))
+                                    int(ignore_index), sc.data_ptr(), gi.data_ptr(), None, ws.data_ptr(),
+                                    ws.numel(), stream)
         _lib.check(st, "vocab_shard_grads")
+        work = grad_input_hook(gi) if grad_input_hook is not None else None
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        reserve = int(os.environ.get("GREYHOUND_B200_COMM_SMS", str(_COMM_SMS)))
+        st = lib.gh_lce_shard_dw(x.data_ptr(), rows, D, Vs, _lib.dtype_code(inputs.dtype), gw.data_ptr(),
+                                 ws.data_ptr(), ws.numel(), max(2, sms - reserve) if work is not None else 0,
+                                 stream)
+        _lib.check(st, "vocab_shard_grads dW")
+        if work is not None:
+            work.wait()
         return gi, gw
     logits = state[1]
     labels = torch.where(target == ignore_index, torch.full_like(target, -(1 << 62)), target)
@@ -324,4 +339,9 @@ def vocab_shard_grads(
         sc.data_ptr(), _lib.stream_of(logits),
     )
     _lib.check(st, "gh_logits_grad")
-    return logits @ weight_shard, logits.T @ inputs
+    gi = logits @ weight_shard
+    work = grad_input_hook(gi) if grad_input_hook is not None else None
+    gw = logits.T @ inputs
+    if work is not None:
+        work.wait()
+    return gi, gw

@@ -228,6 +228,14 @@ GH_API int gh_lce_shard_grads(const void* H, const void* W_shard, const int64_t*
                               void* grad_input_partial, void* grad_weight_shard,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* The shard's grad_weight alone, from the logits gradient that a previous
+ * gh_lce_shard_grads(..., grad_weight_shard = NULL) left in the workspace:
+ * lets the caller start the grad_input all-reduce before this GEMM.
+ * max_ctas <= 0: all SMs. */
+GH_API int gh_lce_shard_dw(const void* H, int64_t N, int64_t D, int64_t V_shard, int dtype,
+                           void* grad_weight_shard, void* workspace, size_t workspace_bytes,
+                           int max_ctas, void* stream);
+
 /* ------------------------------------------------------------------------ *
  * Plain tcgen05 GEMM (the GEMMs of the generic chunked_linear_loss path,
  * src/greyhound/ops/chunked_linear_loss.py:82,94,95-101):

@@ -50,7 +50,8 @@ def cpu_vocab_shard_stats(inputs, weight_shard, target, vocab_start):
     return torch.stack([lse, torch.ones_like(lse), xt], 1), logits
 
 
-def cpu_vocab_shard_grads(inputs, weight_shard, state, target, vocab_start, lse, z, ignore_index, scale):
+def cpu_vocab_shard_grads(inputs, weight_shard, state, target, vocab_start, lse, z, ignore_index, scale,
+                          grad_input_hook=None):
     logits = state
     Vs = weight_shard.shape[0]
     p = torch.exp(logits - lse[:, None]) * (1 + 2 * z * lse)[:, None]
@@ -59,7 +60,12 @@ def cpu_vocab_shard_grads(inputs, weight_shard, state, target, vocab_start, lse,
     p[inside.nonzero()[:, 0], loc[inside]] -= 1.0
     p[target == ignore_index] = 0.0
     p = p * scale.reshape(())
-    return (p @ weight_shard.float()).to(inputs.dtype), (p.T @ inputs.float()).to(weight_shard.dtype)
+    gi = (p @ weight_shard.float()).to(inputs.dtype)
+    work = grad_input_hook(gi) if grad_input_hook is not None else None
+    gw = (p.T @ inputs.float()).to(weight_shard.dtype)
+    if work is not None:
+        work.wait()
+    return gi, gw
 
 
 def _patch():
