@@ -269,3 +269,58 @@ def test_generic_chunked_loss_runs_on_library_gemms_and_matches_oracle():
     assert abs(loss.item() - oloss) <= 1e-3 * abs(oloss)
     assert _maxabs_norm(Hd.grad.float().cpu().numpy(), odH) <= 2e-2
     assert _maxabs_norm(Wd.grad.float().cpu().numpy(), odW) <= 2e-2
+
+
+@requires_gpu
+@pytest.mark.parametrize("case", ["all_ignored", "one_row", "fp16", "tiny_vocab", "ragged"])
+def test_lce_edge_cases_match_oracle(case):
+    """Edge cases of the tcgen05 linear-CE pipeline against the oracle."""
+    N, D, V, dtype, ign = {
+        "all_ignored": (64, 128, 1000, "bf16", 1.0),
+        "one_row": (1, 64, 777, "bf16", 0.0),
+        "fp16": (300, 256, 5000, "f16", 0.1),
+        "tiny_vocab": (40, 64, 3, "bf16", 0.1),
+        "ragged": (257, 136, 4099, "bf16", 0.05),
+    }[case]
+    H, W, t = O.make_lce_inputs(N, D, V, 11, 0.1, ign)
+    if dtype == "f16":
+        H, W = O.round_to(H, "f16"), O.round_to(W, "f16")
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    Hd = _dev(H, tdt).requires_grad_(True)
+    Wd = _dev(W, tdt).requires_grad_(True)
+    loss = chunked_linear_cross_entropy(Hd, Wd, _dev(t), z_loss_multiplier=1e-4)
+    loss.backward()
+    oloss, odH, odW = O.chunked_linear_cross_entropy(H, W, t, -100, "mean", 1e-4, dtype=dtype)
+    assert abs(loss.item() - oloss) <= 1e-3 * max(1.0, abs(oloss))
+    gH = Hd.grad.float().cpu().numpy()
+    gW = Wd.grad.float().cpu().numpy()
+    if case == "all_ignored":
+        assert loss.item() == 0.0
+        assert np.all(gH == 0) and np.all(gW == 0)
+    else:
+        assert _maxabs_norm(gH, odH) <= 2e-2
+        assert _maxabs_norm(gW, odW) <= 2e-2
+    assert np.all(gH[t == -100] == 0)
+
+
+@requires_gpu
+def test_lce_bad_label_is_flagged_not_trapped():
+    """A target outside [0, V) is recorded in the workspace status word and the
+    row is treated as ignored; nothing faults."""
+    from greyhound_b200 import _lib
+
+    N, D, V = 64, 128, 1000
+    H, W, t = O.make_lce_inputs(N, D, V, 3, 0.1, 0.0)
+    t[5] = V + 7
+    Hd, Wd, td = _dev(H, torch.bfloat16), _dev(W, torch.bfloat16), _dev(t)
+    lib = _lib.load()
+    ws = _lib.workspace(lib.gh_lce_workspace_bytes(N, D, V, 0, _lib.GH_BF16, 1), Hd.device)
+    s = [torch.empty((), device=Hd.device) for _ in range(3)]
+    gi = torch.empty_like(Hd)
+    gw = torch.empty_like(Wd)
+    st = lib.gh_lce_fwd_bwd(Hd.data_ptr(), Wd.data_ptr(), td.data_ptr(), N, D, V, _lib.GH_BF16, 0.0, -100, 1, None,
+                            0, 1, 0, gi.data_ptr(), gw.data_ptr(), s[0].data_ptr(), s[1].data_ptr(), s[2].data_ptr(),
+                            ws.data_ptr(), ws.numel(), _lib.stream_of(Hd))
+    _lib.check(st, "lce")
+    assert _lib.device_status(ws) & _lib.GH_DEV_BAD_LABEL
+    assert torch.isfinite(gi).all() and torch.all(gi[5] == 0)
