@@ -367,7 +367,7 @@ def bench_lce(args, rank, world, local):
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        del H, W, Hd
+        del H, W, bufs
         torch.cuda.empty_cache()
         line["cpu_baseline"] = cpu_baseline_lce(N, D, V)
     return line

@@ -46,7 +46,9 @@ enum Epi { EPI_STORE = 0, EPI_LCE = 1 };
 struct Params {
   int M, N, K;
   int num_m, num_n, num_tiles;   // num_m counts tiles of Geo<PAIR>::TM rows
-  int raster;           // 0: m-tile fastest, 1: n-tile fastest
+  int raster;           // 0: m-tile fastest, 1: n-tile fastest,
+                        // 2: groups of `group` m-tiles (m fastest inside), 3: same for n
+  int group;
   // EPI_STORE
   void* out;
   int64_t ldo;
@@ -61,15 +63,35 @@ struct Params {
   float2* stats;          // [num_n][M] (max, sum-exp) in log2 units
   float* xt;              // [M] target logit (written by the tile holding it)
   int* status;            // device error word (bit 2: pipeline timeout)
+  // L2 policy of each operand's TMA loads (0 none, 1 evict_first, 2 evict_last)
+  // and of the epilogue stores (1: evict_first for a large streamed output)
+  int a_hint, b_hint, out_evict_first;
 };
 
+// Tile order. The grouped orders bound how much of the re-read operand is live
+// at once (a group of m-tiles shares one pass over all n-tiles), so it stays
+// in L2 instead of being fetched from DRAM once per band.
 __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, int& nt) {
   if (p.raster == 0) {
     mt = tile % p.num_m;
     nt = tile / p.num_m;
-  } else {
+  } else if (p.raster == 1) {
     nt = tile % p.num_n;
     mt = tile / p.num_n;
+  } else if (p.raster == 2) {
+    const int per = p.group * p.num_n;
+    const int g = tile / per, r = tile % per;
+    const int rem = p.num_m - g * p.group;
+    const int gm = rem < p.group ? rem : p.group;
+    mt = g * p.group + r % gm;
+    nt = r / gm;
+  } else {
+    const int per = p.group * p.num_m;
+    const int g = tile / per, r = tile % per;
+    const int rem = p.num_n - g * p.group;
+    const int gn = rem < p.group ? rem : p.group;
+    nt = g * p.group + r % gn;
+    mt = r / gn;
   }
 }
 
@@ -79,7 +101,8 @@ template <> struct AbType<__half> { static constexpr int v = 0; };
 
 // Store 32 consecutive fp32 values of one output row as OutT.
 template <typename OutT>
-__device__ __forceinline__ void store_row32(OutT* dst, int col0, int N, const float (&v)[32], bool vec_ok) {
+__device__ __forceinline__ void store_row32(OutT* dst, int col0, int N, const float (&v)[32], bool vec_ok,
+                                            bool evict_first = false) {
   constexpr int PER = 16 / sizeof(OutT);
   if (vec_ok && col0 + 32 <= N) {
 #pragma unroll
@@ -89,7 +112,8 @@ __device__ __forceinline__ void store_row32(OutT* dst, int col0, int N, const fl
 #pragma unroll
       for (int k = 0; k < PER; ++k) f[k] = v[q * PER + k];
       o.from_float(f);
-      st16(dst + col0 + q * PER, o.raw);
+      if (evict_first) st16_cs(dst + col0 + q * PER, o.raw);
+      else st16(dst + col0 + q * PER, o.raw);
     }
   } else {
 #pragma unroll
@@ -182,6 +206,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs of a pair) ----------------
+      const uint64_t pol_a = tc::l2_policy(p.a_hint), pol_b = tc::l2_policy(p.b_hint);
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = unit; tile < p.num_tiles; tile += nunits) {
@@ -198,16 +223,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc::mbar_arrive_expect_tx(&full[stage], G::A_BYTES + G::B_BYTES);
             if (A_MN) {
 #pragma unroll
-              for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d(a + j * (BK * 128), &tmA, &full[stage], ma + j * 64, k0);
+              for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d_hint(a + j * (BK * 128), &tmA, &full[stage], ma + j * 64, k0, pol_a);
             } else {
-              tc::tma_load_2d(a, &tmA, &full[stage], k0, ma);
+              tc::tma_load_2d_hint(a, &tmA, &full[stage], k0, ma, pol_a);
             }
             if (B_MN) {
 #pragma unroll
               for (int j = 0; j < G::B_ROWS / 64; ++j)
-                tc::tma_load_2d(b + j * (BK * 128), &tmB, &full[stage], nb + j * 64, k0);
+                tc::tma_load_2d_hint(b + j * (BK * 128), &tmB, &full[stage], nb + j * 64, k0, pol_b);
             } else {
-              tc::tma_load_2d(b, &tmB, &full[stage], k0, nb);
+              tc::tma_load_2d_hint(b, &tmB, &full[stage], k0, nb, pol_b);
             }
           } else {
             // both CTAs' copies complete on the leader's full barrier
@@ -215,16 +240,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             const uint32_t fb = tc::mapa_shared(tc::smem_u32(&full[stage]), 0);
             if (A_MN) {
 #pragma unroll
-              for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d_pair(a + j * (BK * 128), &tmA, fb, ma + j * 64, k0);
+              for (int j = 0; j < BM / 64; ++j) tc::tma_load_2d_pair_hint(a + j * (BK * 128), &tmA, fb, ma + j * 64, k0, pol_a);
             } else {
-              tc::tma_load_2d_pair(a, &tmA, fb, k0, ma);
+              tc::tma_load_2d_pair_hint(a, &tmA, fb, k0, ma, pol_a);
             }
             if (B_MN) {
 #pragma unroll
               for (int j = 0; j < G::B_ROWS / 64; ++j)
-                tc::tma_load_2d_pair(b + j * (BK * 128), &tmB, fb, nb + j * 64, k0);
+                tc::tma_load_2d_pair_hint(b + j * (BK * 128), &tmB, fb, nb + j * 64, k0, pol_b);
             } else {
-              tc::tma_load_2d_pair(b, &tmB, fb, k0, nb);
+              tc::tma_load_2d_pair_hint(b, &tmB, fb, k0, nb, pol_b);
             }
           }
           if (++stage == STG) { stage = 0; phase ^= 1; }
@@ -319,7 +344,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (col0 + j < p.N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
           s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
           m_run = mnew;
-          if (row_ok && p.out) store_row32<OutT>(orow, col0, p.N, x, p.vec_ok);
+          if (row_ok && p.out) store_row32<OutT>(orow, col0, p.N, x, p.vec_ok, p.out_evict_first);
         }
         if (row_ok) p.stats[(int64_t)nt * p.M + row] = make_float2(m_run, s_run);
       } else {
@@ -348,7 +373,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += a[j];
             }
-            store_row32<OutT>(orow, col0, p.N, v, p.vec_ok);
+            store_row32<OutT>(orow, col0, p.N, v, p.vec_ok, p.out_evict_first);
           }
         }
       }
