@@ -39,7 +39,12 @@ sys.path.insert(0, str(ROOT))
 METRIC = "linear-CE fwd+bwd tokens/s, Llama-3-8B head; % bf16 TC peak @1/2/4/8 GPU"
 # DRAM bytes (read + write) per launch from one ncu capture of each kernel class
 # at the bench workload (profiles/*.md); None until captured.
-TRAFFIC_BYTES_PER_LAUNCH: dict = {}
+TRAFFIC_BYTES_PER_LAUNCH: dict = {
+    # profiles/tc_gemm_cfg3_traffic.md (cfg3, one chunk): read + write
+    "gemm_logits_ce": 4.15e9 + 2.11e9,
+    "gemm_dw": 18.28e9 + 1.04e9,
+    "gemm_dh": 21.68e9 + 0.063e9,
+}
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
