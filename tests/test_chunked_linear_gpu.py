@@ -324,3 +324,49 @@ def test_lce_bad_label_is_flagged_not_trapped():
     _lib.check(st, "lce")
     assert _lib.device_status(ws) & _lib.GH_DEV_BAD_LABEL
     assert torch.isfinite(gi).all() and torch.all(gi[5] == 0)
+
+
+@requires_gpu
+def test_lce_cfg3_full_size_against_torch_fp32():
+    """Workload cfg3 at full size (8192 x 4096 x 128256, bf16, 2% ignore, mean):
+    loss within 1e-3 relative and both gradients within 2e-2 (max-abs after
+    normalising by the reference's max) of a plain-torch fp32 computation of the
+    reference semantics (bf16 logits, fp32 softmax / CE, fp32 GEMMs)."""
+    dev = get_default_device()
+    g = torch.Generator(device=dev).manual_seed(2)
+    N, D, V = 8192, 4096, 128256
+    H = torch.randn(N, D, device=dev, generator=g)
+    H = (H * torch.rsqrt(H.square().mean(-1, keepdim=True) + 1e-6)).bfloat16()
+    W = (torch.randn(V, D, device=dev, generator=g) * 0.02).bfloat16()
+    t = torch.randint(0, V, (N,), device=dev, generator=g)
+    t[torch.rand(N, device=dev, generator=g) < 0.02] = -100
+    Hd = H.clone().requires_grad_(True)
+    Wd = W.clone().requires_grad_(True)
+    loss = chunked_linear_cross_entropy(Hd, Wd, t)
+    loss.backward()
+    # reference semantics in fp32 torch (chunked to bound memory)
+    valid = t != -100
+    n = valid.sum().float()
+    ref_loss = torch.zeros((), device=dev, dtype=torch.float64)
+    ref_dH = torch.empty(N, D, device=dev)
+    ref_dW = torch.zeros(V, D, device=dev)
+    Wf = W.float()
+    for s in range(0, N, 2048):
+        logits = (H[s:s + 2048] @ W.T).float()  # bf16 logits, as the reference GEMM output
+        lse = torch.logsumexp(logits, -1)
+        tc = t[s:s + 2048]
+        vc = tc != -100
+        ref_loss += torch.where(vc, lse - logits.gather(1, tc.clamp(min=0)[:, None])[:, 0], 0.0).double().sum()
+        dl = torch.softmax(logits, -1)
+        dl[vc.nonzero()[:, 0], tc[vc]] -= 1.0
+        dl[~vc] = 0.0
+        dl = dl.bfloat16().float() / n  # the kernel's bf16 dlogits
+        ref_dH[s:s + 2048] = dl @ Wf
+        ref_dW += dl.T @ H[s:s + 2048].float()
+        del logits, dl
+    ref_loss = (ref_loss / n).item()
+    assert abs(loss.item() - ref_loss) <= 1e-3 * abs(ref_loss)
+    for got, ref in ((Hd.grad, ref_dH), (Wd.grad, ref_dW)):
+        err = (got.float() - ref).abs().max() / ref.abs().max()
+        assert err <= 2e-2, err.item()
+    assert torch.all(Hd.grad[~valid] == 0)
