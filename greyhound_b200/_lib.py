@@ -21,6 +21,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgreyhound_b200.so"
 GH_F16, GH_BF16, GH_F32, GH_I32, GH_I64 = 0, 1, 2, 3, 4
 GH_OK, GH_EINVAL, GH_ETYPE, GH_ECUDA, GH_EWORKSPACE, GH_EUNSUPPORTED = 0, 1, 2, 3, 4, 5
 GH_DEV_BAD_LABEL = 1
+GH_DEV_PIPELINE_TIMEOUT = 4
 
 DTYPE_CODE = {
     torch.float16: GH_F16,
@@ -71,6 +72,7 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _i64, _i32, _vp, _i64, _i32, _i64, _i64, _i64, _i32, _vp, _i64, _i32, _vp, _i64, _vp, _vp, _vp],
     ),
     "gh_scale": (_i32, [_vp, _vp, _i64, _i32, _vp, _vp]),
+    "gh_gemm_selftest_stall": (_i32, [_vp, _sz, _vp, _i32, _vp]),
     "gh_lce_shard_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
     "gh_lce_shard_stats": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _sz, _vp]),
     "gh_lce_shard_dw": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _sz, _i32, _vp]),

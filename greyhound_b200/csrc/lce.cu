@@ -673,3 +673,27 @@ extern "C" int gh_lce_shard_dw(const void* H, int64_t N, int64_t D, int64_t V_sh
                   D, nullptr, nullptr, 0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream),
                   reinterpret_cast<int*>(ws + L.status), PROF_GEMM_DW, kStreamA_KeepB);
 }
+
+extern "C" int gh_gemm_selftest_stall(void* scratch, size_t scratch_bytes, int* status, int wait_ms, void* stream) {
+  if (!scratch || !status || scratch_bytes < (size_t)(128 * 64 + 256 * 64 + 128 * 256) * 2)
+    return set_error(GH_EINVAL, "gh_gemm_selftest_stall: scratch of at least 112 KB and a status word are required");
+  if ((reinterpret_cast<uintptr_t>(scratch) & 15)) return set_error(GH_EINVAL, "scratch must be 16-byte aligned");
+  if (wait_ms <= 0 || wait_ms > 10000) return set_error(GH_EINVAL, "wait_ms must be in (0, 10000]");
+  char* base = static_cast<char*>(scratch);
+  CUtensorMap ta, tb;
+  int rc = make_operand_maps(&ta, &tb, GH_BF16, Operand{base, 64, 0}, Operand{base + 128 * 64 * 2, 64, 0}, 128, 256,
+                             64, 1);
+  if (rc) return rc;
+  gemm::Params p{};
+  set_tiles(p, 128, 256, 64, 1);
+  p.raster = 0;
+  p.group = 1;
+  p.out = base + (128 * 64 + 256 * 64) * 2;
+  p.ldo = 256;
+  p.vec_ok = 1;
+  p.status = status;
+  p.wait_limit_ns = (uint64_t)wait_ms * 1000000ull;
+  p.debug_no_loads = 1;
+  return launch_gemm_t<__nv_bfloat16, 0, 0, gemm::EPI_STORE, __nv_bfloat16, 1>(ta, tb, p, 1,
+                                                                              static_cast<cudaStream_t>(stream));
+}

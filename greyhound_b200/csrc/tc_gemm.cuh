@@ -66,6 +66,11 @@ struct Params {
   // L2 policy of each operand's TMA loads (0 none, 1 evict_first, 2 evict_last)
   // and of the epilogue stores (1: evict_first for a large streamed output)
   int a_hint, b_hint, out_evict_first;
+  // Pipeline wait limit (0: 10 s). Self-test only: debug_no_loads makes the
+  // producer issue nothing, so the waits run out and the kernel must return
+  // with status bit 4 instead of hanging.
+  uint64_t wait_limit_ns;
+  int debug_no_loads;
 };
 
 // Tile order. The grouped orders bound how much of the re-read operand is live
@@ -202,6 +207,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   tc::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const int nkb = (p.K + BK - 1) / BK;
+  const uint64_t lim = p.wait_limit_ns ? p.wait_limit_ns : 10000000000ull;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -209,13 +215,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const uint64_t pol_a = tc::l2_policy(p.a_hint), pol_b = tc::l2_policy(p.b_hint);
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = unit; tile < p.num_tiles; tile += nunits) {
+      for (int tile = p.debug_no_loads ? p.num_tiles : unit; tile < p.num_tiles; tile += nunits) {
         int mt, nt;
         tile_coords(p, tile, mt, nt);
         const int ma = mt * G::TM + (int)rank * BM;         // this CTA's A rows
         const int nb = nt * BN + (int)rank * G::B_ROWS;     // this CTA's B rows
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag)) goto producer_done;
+          if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, lim)) goto producer_done;
           uint8_t* a = sA + stage * G::A_BYTES;
           uint8_t* b = sB + stage * G::B_BYTES;
           const int k0 = kb * BK;
@@ -272,12 +278,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int tile = unit; tile < p.num_tiles; tile += nunits) {
-        if (!tc::mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) break;
+        if (!tc::mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, lim)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
-          if (!tc::mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          if (!tc::mbar_wait(&full[stage], phase, abort_flag, lim)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t a0 = tc::smem_u32(sA + stage * G::A_BYTES);
           const uint32_t b0 = tc::smem_u32(sB + stage * G::B_BYTES);
@@ -309,7 +315,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int mt, nt;
       tile_coords(p, tile, mt, nt);
       const int m0 = mt * G::TM + (int)rank * BM, n0 = nt * BN;
-      if (!tc::mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      if (!tc::mbar_wait(&tfull[acc], acc_phase, abort_flag, lim)) break;
       tc::tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < p.M;

@@ -269,6 +269,16 @@ GH_API int gh_scale(const void* in, void* out, int64_t n, int dtype, const float
 GH_API void gh_profile_enable(int on);
 GH_API int gh_profile_read(double* ms_out, long long* count_out, int n_classes, int reset);
 
+/* Failure-detection self-test of the GEMM pipeline (no counterpart in the
+ * reference): launches one small GEMM whose load stage deliberately issues
+ * nothing, with all pipeline waits limited to wait_ms. The kernel must give
+ * up, free its tensor memory, set bit 4 (GH_DEV_PIPELINE_TIMEOUT) in *status
+ * (device int, caller-zeroed) and return, leaving the context usable.
+ * scratch: >= 112 KB of device memory used only to describe the operands. */
+enum { GH_DEV_PIPELINE_TIMEOUT = 4 };
+GH_API int gh_gemm_selftest_stall(void* scratch, size_t scratch_bytes, int* status, int wait_ms,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

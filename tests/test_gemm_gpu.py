@@ -51,3 +51,28 @@ def test_gemm_addend_and_scale():
     ref = accb.float() + a.float() @ b.float().T
     out = gemm_nt(a, b, out=accb, addend=accb)
     assert _rel(out.float(), ref) < 1e-2
+
+
+@requires_gpu
+def test_gemm_pipeline_timeout_returns_with_status():
+    """Failure detection without a GPU fault: a GEMM whose loads never arrive
+    gives up after a short bounded wait, reports GH_DEV_PIPELINE_TIMEOUT and
+    returns; the context keeps working (a normal GEMM afterwards is correct)."""
+    import time
+
+    from greyhound_b200 import _lib
+
+    lib = _lib.load()
+    scratch = torch.zeros(128 * 1024, dtype=torch.uint8, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t0 = time.time()
+    st = lib.gh_gemm_selftest_stall(scratch.data_ptr(), scratch.numel(), status.data_ptr(), 50,
+                                    torch.cuda.current_stream().cuda_stream)
+    _lib.check(st, "selftest")
+    torch.cuda.synchronize()
+    assert time.time() - t0 < 30
+    assert int(status.item()) & _lib.GH_DEV_PIPELINE_TIMEOUT
+    a = torch.randn(256, 512, device="cuda").bfloat16()
+    b = torch.randn(384, 512, device="cuda").bfloat16()
+    out = gemm_nt(a, b, out_dtype=torch.float32)
+    assert _rel(out, a.float() @ b.float().T) < 1e-5
