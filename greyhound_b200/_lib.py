@@ -11,6 +11,7 @@ devices and layouts, TypeError for dtypes).
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
@@ -186,3 +187,20 @@ def scaled(t: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
     check(load().gh_scale(t.data_ptr(), out.data_ptr(), t.numel(), dtype_code(t.dtype), gf.data_ptr(),
                           stream_of(t)), "scale")
     return out
+
+
+CHECK_STATUS = os.environ.get("GREYHOUND_B200_CHECK", "0") not in ("", "0")
+
+
+def raise_on_status(ws: torch.Tensor, what: str) -> None:
+    """With GREYHOUND_B200_CHECK=1: synchronise and raise if the kernels of the
+    last call recorded a problem in the workspace status word (a label outside
+    [0, V): ValueError; a pipeline timeout: RuntimeError). Off by default: the
+    status word is written on the device and reading it costs a host sync."""
+    if not CHECK_STATUS:
+        return
+    st = device_status(ws)
+    if st & GH_DEV_BAD_LABEL:
+        raise ValueError(f"{what}: a target / index outside [0, vocab) that is not ignore_index")
+    if st:
+        raise GreyhoundLibraryError(f"{what}: device status {st:#x} (pipeline timeout)")

@@ -87,6 +87,7 @@ def cross_entropy_with_grad(
         _lib.stream_of(logits),
     )
     _lib.check(status, "cross_entropy_with_grad")
+    _lib.raise_on_status(ws, "cross_entropy_with_grad")
     return ce_sum, z_sum, n_valid
 
 

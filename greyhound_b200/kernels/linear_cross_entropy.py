@@ -111,6 +111,7 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
         ws.data_ptr(), ws.numel(), stream,
     )
     _lib.check(st, "linear_cross_entropy")
+    _lib.raise_on_status(ws, "linear_cross_entropy")
     if defer:
         work = grad_weight_hook(gw)
         # The last chunk's dH runs in two parts: the first on fewer SMs, so the

@@ -71,6 +71,7 @@ def selective_log_softmax_with_lse(
         _lib.stream_of(logits),
     )
     _lib.check(status, "selective_log_softmax")
+    _lib.raise_on_status(ws, "selective_log_softmax")
     return out, lse
 
 

@@ -229,3 +229,13 @@ def test_cfg2_full_size_properties(rows):
         c, _, _, _ = O.cross_entropy_with_grad(x[s:s + 512], t[s:s + 512], 0.0, -100)
         tot += c
     assert abs(ce.item() - tot) <= 1e-3 * abs(tot)
+
+
+@requires_gpu
+def test_check_mode_raises_on_bad_label(monkeypatch):
+    """GREYHOUND_B200_CHECK=1 turns the device status word into an exception."""
+    monkeypatch.setattr(_lib, "CHECK_STATUS", True)
+    x = torch.randn(4, 100, device=get_default_device(), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="outside"):
+        cross_entropy(x, torch.tensor([1, 200, -100, 3], device=x.device))
+    assert cross_entropy(x, torch.tensor([1, 2, -100, 3], device=x.device)).isfinite()
