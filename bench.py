@@ -38,9 +38,9 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "linear-CE fwd+bwd tokens/s, Llama-3-8B head; % bf16 TC peak @1/2/4/8 GPU"
 # DRAM bytes (read + write) per launch from one ncu capture of each kernel class
-# at the bench workload (profiles/*.md); None until captured.
+# at the bench workload (one-pass ncu capture of each GEMM class); None if not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict = {
-    # profiles/tc_gemm_cfg3_traffic.md (cfg3, one chunk): read + write
+    # Llama-3-8B head, one chunk: DRAM read + write per launch
     "gemm_logits_ce": 4.15e9 + 2.11e9,
     "gemm_dw": 18.28e9 + 1.04e9,
     "gemm_dh": 21.68e9 + 0.063e9,
@@ -379,7 +379,7 @@ def bench_lce(args, rank, world, local):
 
 
 def bench_lce70b(args, rank, world, local):
-    """Llama-3-70B-scale head, H[65536, 8192], W[128256, 8192]
+    """Llama-3-70B-scale head workload: H[65536, 8192], W[128256, 8192]
     ~N(0, 0.015), 2% ignore, mean. ``--parallel rows``: the 65536 rows split over
     the ranks, W replicated, dW all-reduced; ``--parallel vocab``: W split by
     vocabulary rows, H replicated, per-row statistics all-gathered and the
