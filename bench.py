@@ -190,6 +190,9 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
+_CPU_W: dict = {}
+
+
 def cpu_baseline_lce(N, D, V, budget_s=12.0, rows_per_sample=64):
     """Oracle (numpy, fp32 BLAS on all host threads) on row samples of the workload."""
     import numpy as np
@@ -197,9 +200,13 @@ def cpu_baseline_lce(N, D, V, budget_s=12.0, rows_per_sample=64):
     from oracle import gh_oracle as O
 
     rng = np.random.default_rng(2)
-    gen = torch.Generator().manual_seed(2)
-    W = (torch.randn(V, D, generator=gen) * 0.02).to(torch.bfloat16).float().numpy()
-    acc = np.zeros((D, V), dtype=np.float32)  # fp32 weight-gradient accumulator, as the reference
+    key = (V, D)
+    if key not in _CPU_W:  # the weight and its fp32 gradient accumulator, built once per process
+        gen = torch.Generator().manual_seed(2)
+        W = (torch.randn(V, D, generator=gen) * 0.02).to(torch.bfloat16).float().numpy()
+        _CPU_W.clear()
+        _CPU_W[key] = (W, np.zeros((D, V), dtype=np.float32))
+    W, acc = _CPU_W[key]
     done = 0
     t0 = time.perf_counter()
     while True:
@@ -550,7 +557,7 @@ def main() -> int:
     ap.add_argument("--workload", choices=["lce", "lce70b", "ce", "sls", "sls_bwd"], default="lce")
     ap.add_argument("--parallel", choices=["rows", "vocab"], default="rows", help="lce70b sharding mode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ref-step-seconds", type=float, default=8.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=5.0)
     # shape overrides, only for small profiler captures (the default is the workload)
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--hidden", type=int, default=0)
