@@ -65,7 +65,7 @@ ce_fused_kernel(const T* __restrict__ logits, T* dlogits, const int64_t* __restr
       } else {
         const float scale = scale_ptr ? *scale_ptr : 1.f;
         const float coef = scale * (1.f + 2.f * zmul * lse) / tot.s;
-        row_grad<T, THREADS, UNROLL>(x, y, V, lab, tot.m, coef, scale);
+        row_grad<T, THREADS, UNROLL, true>(x, y, V, lab, tot.m, coef, scale);
       }
     }
   }

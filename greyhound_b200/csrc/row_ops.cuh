@@ -52,7 +52,9 @@ __device__ __forceinline__ MS row_partial(const T* __restrict__ x, int64_t n) {
 
 // y[c] = exp2(x[c] * log2e - mm) * coef - (c == lab ? sub : 0) for c in [0, n).
 // x and y share their 16-byte misalignment (checked on the host). y may be x.
-template <typename T, int THREADS, int UNROLL>
+// REV: walk the vectors from the end of the row, i.e. re-read first what the
+// preceding pass loaded last (the lines most likely still in L2).
+template <typename T, int THREADS, int UNROLL, bool REV = false>
 __device__ __forceinline__ void row_grad(const T* x, T* y, int64_t n, int64_t lab,
                                          float mm, float coef, float sub) {
   constexpr int PER = 32 / sizeof(T);
@@ -71,42 +73,43 @@ __device__ __forceinline__ void row_grad(const T* x, T* y, int64_t n, int64_t la
   // vector holding the label (or -1): one compare per vector, not per element
   const int64_t lab_vec = (lab_rel >= 0 && lab_rel < sp.nvec * PER) ? lab_rel / PER : -1;
   const int lab_k = (int)(lab_rel - (lab_vec < 0 ? 0 : lab_vec) * PER);
+  auto vi = [&](int64_t j) { return REV ? sp.nvec - 1 - j : j; };
   int64_t i = tid;
   for (; i + (int64_t)(UNROLL - 1) * THREADS < sp.nvec; i += (int64_t)UNROLL * THREADS) {
     Vec32<T> r[UNROLL];
 #pragma unroll
-    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld32_last(xv + i + u * THREADS);
+    for (int u = 0; u < UNROLL; ++u) r[u].raw = ld32_last(xv + vi(i + u * THREADS));
 #pragma unroll
     for (int u = 0; u < UNROLL; ++u) {
       float f[PER];
       r[u].to_float(f);
 #pragma unroll
       for (int k = 0; k < PER; ++k) f[k] = fast_exp2(fmaf(f[k], kLog2e, -mm)) * coef;
-      if (i + u * THREADS == lab_vec) {
+      if (vi(i + u * THREADS) == lab_vec) {
 #pragma unroll
         for (int k = 0; k < PER; ++k)
           if (k == lab_k) f[k] -= sub;
       }
       Vec32<T> o;
       o.from_float(f);
-      st32_stream(yv + i + u * THREADS, o.raw);
+      st32_stream(yv + vi(i + u * THREADS), o.raw);
     }
   }
   for (; i < sp.nvec; i += THREADS) {
     Vec32<T> r;
-    r.raw = ld32_last(xv + i);
+    r.raw = ld32_last(xv + vi(i));
     float f[PER];
     r.to_float(f);
 #pragma unroll
     for (int k = 0; k < PER; ++k) f[k] = fast_exp2(fmaf(f[k], kLog2e, -mm)) * coef;
-    if (i == lab_vec) {
+    if (vi(i) == lab_vec) {
 #pragma unroll
       for (int k = 0; k < PER; ++k)
         if (k == lab_k) f[k] -= sub;
     }
     Vec32<T> o;
     o.from_float(f);
-    st32_stream(yv + i, o.raw);
+    st32_stream(yv + vi(i), o.raw);
   }
 }
 
