@@ -86,10 +86,10 @@ struct Operand {
   int mn_major;  // 0: [rows, K] K contiguous; 1: [K, rows] rows contiguous
 };
 
-template <typename T, int A_MN, int B_MN, int EPI, typename OutT, int PAIR>
+template <typename T, int A_MN, int B_MN, int EPI, typename OutT, int PAIR, int NSUB = 1>
 int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p, int max_ctas, cudaStream_t st) {
-  auto kern = gemm::tc_gemm_kernel<T, A_MN, B_MN, EPI, OutT, PAIR>;
-  constexpr int SMEM = gemm::Geo<PAIR>::SMEM;
+  auto kern = gemm::tc_gemm_kernel<T, A_MN, B_MN, EPI, OutT, PAIR, NSUB>;
+  constexpr int SMEM = gemm::Geo<PAIR, NSUB>::SMEM;
   static int max_units[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -139,10 +139,21 @@ int launch_gemm_t(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p,
   return check_launch("tc_gemm");
 }
 
-// Dispatch on majorness and pairing for a fixed (T, EPI, OutT).
+// Dispatch on majorness, pairing and tile width for a fixed (T, EPI, OutT).
 template <typename T, int EPI, typename OutT>
-int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b_mn, int pair, gemm::Params& p,
-                   int max_ctas, cudaStream_t st) {
+int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b_mn, int pair, int nsub,
+                   gemm::Params& p, int max_ctas, cudaStream_t st) {
+  if (pair == 2 && nsub == 2) {
+    if constexpr (sizeof(OutT) == 2) {
+      if (p.add_f32 || p.add_same) return set_error(GH_EUNSUPPORTED, "512-column GEMM tile with an addend");
+      if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT, 2, 2>(ta, tb, p, max_ctas, st);
+      if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT, 2, 2>(ta, tb, p, max_ctas, st);
+      if (a_mn && !b_mn) return launch_gemm_t<T, 1, 0, EPI, OutT, 2, 2>(ta, tb, p, max_ctas, st);
+      return launch_gemm_t<T, 1, 1, EPI, OutT, 2, 2>(ta, tb, p, max_ctas, st);
+    } else {
+      return set_error(GH_EUNSUPPORTED, "512-column GEMM tile with an fp32 output");
+    }
+  }
   if (pair == 2) {
     if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT, 2>(ta, tb, p, max_ctas, st);
     if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT, 2>(ta, tb, p, max_ctas, st);
@@ -158,6 +169,38 @@ int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b
 // 2-CTA tiles (256 rows) once there are more than 128 rows.
 inline int pick_pair(int64_t M) { return M > BM ? 2 : 1; }
 
+// Tile width of a paired GEMM: 512 columns (NSUB = 2) unless the coarser
+// tiles would leave a last wave much emptier than 256-column tiles do. The
+// wide tile is credited with 6 % (its measured energy saving at the power
+// cap). Outputs that need an fp32 epilogue (fp32 output, an addend) keep 256
+// columns: only 16-bit outputs can be parked in registers to free TMEM early.
+// The linear-CE epilogue (logits + statistics, ~4k cycles per 32-column chunk
+// next to the MMAs) also keeps 256 columns: with 512 the tensor pipe waited
+// ~18 % of each tile for it (measured), while two 256-column accumulators
+// hide it completely. GREYHOUND_B200_GEMM_WIDE=0 forces 256 columns, =2
+// forces 512 wherever the output allows it.
+inline int wide_mode() {
+  static int mode = [] {
+    const char* e = getenv("GREYHOUND_B200_GEMM_WIDE");
+    return e && *e ? atoi(e) : 1;
+  }();
+  return mode;
+}
+inline int pick_nsub(int64_t M, int64_t N, int pair, int units, bool fp32_epilogue, bool lce_epilogue) {
+  if (pair != 2 || N <= BN || fp32_epilogue) return 1;
+  const int mode = wide_mode();
+  if (mode != 1) return mode == 2 ? 2 : 1;
+  if (lce_epilogue) return 1;
+  auto eff = [&](int64_t tn) {
+    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + tn - 1) / tn);
+    const int64_t waves = (tiles + units - 1) / units;
+    // useful columns per computed column (a partial last tile computes zeros)
+    const double fill = (double)N / (double)(((N + tn - 1) / tn) * tn);
+    return (double)tiles / (double)(waves * units) * fill;
+  };
+  return eff(2 * BN) * 1.06 >= eff(BN) ? 2 : 1;
+}
+
 // Tensor maps of both operands for a GEMM of M x N x K with pairing `pair`.
 int make_operand_maps(CUtensorMap* ta, CUtensorMap* tb, int dtype, const Operand& A, const Operand& B, int64_t M,
                       int64_t N, int64_t K, int pair) {
@@ -170,12 +213,12 @@ int make_operand_maps(CUtensorMap* ta, CUtensorMap* tb, int dtype, const Operand
   return rc;
 }
 
-void set_tiles(gemm::Params& p, int64_t M, int64_t N, int64_t K, int pair) {
+void set_tiles(gemm::Params& p, int64_t M, int64_t N, int64_t K, int pair, int nsub = 1) {
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
   p.num_m = (int)((M + BM * pair - 1) / (BM * pair));
-  p.num_n = (int)((N + BN - 1) / BN);
+  p.num_n = (int)((N + BN * nsub - 1) / (BN * nsub));
   p.num_tiles = p.num_m * p.num_n;
 }
 
@@ -202,14 +245,18 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
              const float* scale, int raster, int max_ctas, cudaStream_t st, int* status,
              int prof_class = PROF_GEMM_OTHER, Hints hints = Hints{}) {
   if (M <= 0 || N <= 0) return GH_OK;
+  if (K <= 0) return set_error(GH_EINVAL, "GEMM needs K >= 1");
   ProfScope prof(prof_class, st);
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return set_error(GH_EINVAL, "GEMM dimension too large");
   const int pair = pick_pair(M);
+  int units = num_sms_dev() / 2;
+  if (max_ctas > 0 && max_ctas / 2 < units) units = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+  const int nsub = pick_nsub(M, N, pair, units, out_dtype == GH_F32 || add_f32 || add_same, false);
   CUtensorMap ta, tb;
   int rc = make_operand_maps(&ta, &tb, dtype, A, B, M, N, K, pair);
   if (rc) return rc;
   gemm::Params p{};
-  set_tiles(p, M, N, K, pair);
+  set_tiles(p, M, N, K, pair, nsub);
   p.raster = raster;
   p.group = 1;
   p.out = out;
@@ -227,11 +274,11 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
   p.b_hint = hints.b;
   p.out_evict_first = hints.out;
   if (dtype == GH_BF16) {
-    if (out_dtype == GH_F32) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
-    if (out_dtype == GH_BF16) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
+    if (out_dtype == GH_F32) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
+    if (out_dtype == GH_BF16) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
   } else if (dtype == GH_F16) {
-    if (out_dtype == GH_F32) return launch_gemm_mm<__half, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
-    if (out_dtype == GH_F16) return launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, pair, p, max_ctas, st);
+    if (out_dtype == GH_F32) return launch_gemm_mm<__half, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
+    if (out_dtype == GH_F16) return launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
   }
   return set_error(GH_ETYPE, "unsupported GEMM dtype combination (%d -> %d)", dtype, out_dtype);
 }
@@ -401,11 +448,12 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
     // 1. logits GEMM + fused CE statistics
     {
       const int pair = pick_pair(rows);
+      const int nsub = pick_nsub(rows, V, pair, sms / 2, false, true);
       CUtensorMap ta, tb;
       if ((rc = make_operand_maps(&ta, &tb, dtype, Operand{Hc, D, 0}, Operand{W, D, 0}, rows, V, D, pair)))
         return rc;
       gemm::Params p{};
-      set_tiles(p, rows, V, D, pair);
+      set_tiles(p, rows, V, D, pair, nsub);
       p.raster = 2;
       p.group = kLogitsGroup;
       p.out = with_grad ? logits : nullptr;  // forward only: statistics, no logits
@@ -419,8 +467,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       p.xt = xt;
       p.status = status;
       ProfScope prof(PROF_GEMM_LOGITS_CE, st);
-      if (pair == 2) rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 2>(ta, tb, p, sms, st);
-      else rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 1>(ta, tb, p, sms, st);
+      rc = launch_gemm_mm<T, gemm::EPI_LCE, T>(ta, tb, 0, 0, pair, nsub, p, sms, st);
       if (rc) return rc;
     }
     // 2. per-row logsumexp and loss terms
@@ -480,11 +527,12 @@ int shard_stats_run(const void* H, const void* W, const int64_t* target, int64_t
   float* xt = reinterpret_cast<float*>(ws + L.xt);
   cudaMemsetAsync(status, 0, sizeof(int), st);
   const int pair = pick_pair(N);
+  const int nsub = pick_nsub(N, Vs, pair, num_sms_dev() / 2, false, true);
   CUtensorMap ta, tb;
   int rc;
   if ((rc = make_operand_maps(&ta, &tb, dtype, Operand{H, D, 0}, Operand{W, D, 0}, N, Vs, D, pair))) return rc;
   gemm::Params p{};
-  set_tiles(p, N, Vs, D, pair);
+  set_tiles(p, N, Vs, D, pair, nsub);
   p.raster = 2;
   p.group = kLogitsGroup;
   p.out = logits;
@@ -500,8 +548,7 @@ int shard_stats_run(const void* H, const void* W, const int64_t* target, int64_t
   p.status = status;
   {
     ProfScope prof(PROF_GEMM_LOGITS_CE, st);
-    if (pair == 2) rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 2>(ta, tb, p, num_sms_dev(), st);
-    else rc = launch_gemm_t<T, 0, 0, gemm::EPI_LCE, T, 1>(ta, tb, p, num_sms_dev(), st);
+    rc = launch_gemm_mm<T, gemm::EPI_LCE, T>(ta, tb, 0, 0, pair, nsub, p, num_sms_dev(), st);
     if (rc) return rc;
   }
   lce_combine_kernel<<<(unsigned)((N + 31) / 32), 32 * kCombineWarps, 0, st>>>(

@@ -9,16 +9,20 @@
 //   dH      = dlogits @ W    A = dlogits [C, V] K-major,  B = W [V, D] MN-major
 //   dW      = dlogits^T @ H  A = dlogits [C, V] MN-major, B = H [C, D] MN-major
 //
-// CTA: 256 threads, one CTA per SM, persistent over output tiles of
-// 128 x 256 (static round-robin over a rasterised tile order).
-//   warp 0      TMA producer: 4-stage ring of (A 128x64, B 256x64) tiles,
+// CTA: 320 threads, one CTA per SM, persistent over output tiles of
+// 128 x 256 (static round-robin over a rasterised tile order); CTA pairs
+// (cta_group::2) share 256 x 256 or 256 x 512 tiles (see Geo below).
+//   warp 0      TMA producer: ring of (A 128x64, B 256x64) stages,
 //               128-byte swizzle, completion on mbarriers
-//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=16) per stage,
+//   warp 1      MMA issuer: 4 x tcgen05.mma (K=16) per stage and accumulator,
 //               tcgen05.commit frees the smem stage / publishes the tile
-//   warp 2      TMEM allocator (512 columns = two 128x256 fp32 accumulators)
-//   warps 4-7   epilogue: tcgen05.ld (32 lanes x 32 columns) -> registers ->
-//               fused epilogue -> global; double-buffered TMEM lets the
-//               epilogue of tile i overlap the MMAs of tile i+1
+//   warps 2-9   epilogue: tcgen05.ld (32 lanes x 32 columns) -> registers ->
+//               fused epilogue -> global (stores staged through shared
+//               memory so each instruction writes whole row segments);
+//               double-buffered TMEM lets the epilogue of tile i overlap the
+//               MMAs of tile i+1. Warp 2 also allocates TMEM (512 columns =
+//               two 128x256 fp32 accumulators, or the two halves of one
+//               128x512 accumulator).
 // Epilogues: plain store (optional scale and fp32 / same-type addend), or the
 // linear-CE epilogue (bf16 logits + per-(row, 256-column tile) max / sum-exp
 // + target logit), which replaces the reference's separate CE row pass
@@ -38,7 +42,10 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;           // 64 x 2 B = one 128-byte swizzle row
-constexpr int THREADS = 256;
+constexpr int THREADS = 320;     // warp 0 producer, 1 MMA, 2-9 epilogue (warp 2 also owns TMEM)
+constexpr int EPI_WARP0 = 2;
+constexpr int EPI_WARPS = 8;
+constexpr int EPI_CHUNKS = BN / 32 / (EPI_WARPS / 4);  // 32-column chunks per warp per half
 constexpr int TMEM_COLS = 2 * BN;
 
 enum Epi { EPI_STORE = 0, EPI_LCE = 1 };
@@ -146,24 +153,169 @@ __device__ __forceinline__ void load_row32(const OutT* src, int col0, int N, flo
   }
 }
 
+// Store one warp's 32 rows x 32 columns (lane = row, v = that row's values)
+// through a 2 KB shared-memory transpose, so each global store instruction
+// writes 8 rows x 64 contiguous bytes instead of 32 rows x 16 bytes. The 16-byte
+// pieces of a row are XOR-swizzled by (row >> 1) & 3, which keeps both the
+// row-wise writes and the column-wise reads free of bank conflicts. Ragged
+// column edges and unaligned outputs take the per-row path.
+template <typename OutT>
+__device__ __forceinline__ void store_chunk(OutT* out, int64_t ldo, int row0, int M, int col0, int N,
+                                            const float (&v)[32], uint8_t* buf, int lane, bool vec_ok,
+                                            bool evict_first) {
+  constexpr int PER = 16 / sizeof(OutT);  // elements per 16-byte piece
+  constexpr int PASSES = 32 / PER / 4;    // 4 pieces (64 B) per row per pass
+  if (!vec_ok || col0 + 32 > N) {
+    if (row0 + lane < M) store_row32<OutT>(out + (int64_t)(row0 + lane) * ldo, col0, N, v, vec_ok, evict_first);
+    return;
+  }
+#pragma unroll
+  for (int pass = 0; pass < PASSES; ++pass) {
+#pragma unroll
+    for (int pc = 0; pc < 4; ++pc) {
+      Vec16<OutT> o;
+      float f[PER];
+#pragma unroll
+      for (int k = 0; k < PER; ++k) f[k] = v[(pass * 4 + pc) * PER + k];
+      o.from_float(f);
+      *reinterpret_cast<uint4*>(buf + lane * 64 + 16 * (pc ^ ((lane >> 1) & 3))) = o.raw;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = j * 8 + (lane >> 2), pc = lane & 3;
+      const uint4 w = *reinterpret_cast<const uint4*>(buf + r * 64 + 16 * (pc ^ ((r >> 1) & 3)));
+      if (row0 + r < M) {
+        OutT* dst = out + (int64_t)(row0 + r) * ldo + col0 + (pass * 4 + pc) * PER;
+        if (evict_first) st16_cs(dst, w);
+        else st16(dst, w);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Two values rounded to a 16-bit type and packed into one word (first value
+// in the low half), and the inverse.
+template <typename OutT> __device__ __forceinline__ uint32_t pack2(float a, float b);
+template <> __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+template <typename OutT> __device__ __forceinline__ void unpack2(uint32_t w, float& a, float& b);
+template <> __device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& a, float& b) {
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xffff0000u);
+}
+template <> __device__ __forceinline__ void unpack2<__half>(uint32_t w, float& a, float& b) {
+  asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+      : "=f"(a), "=f"(b)
+      : "r"(w));
+}
+
+// store_chunk for 32 already-packed 16-bit values per row (w: 16 words).
+template <typename OutT>
+__device__ __forceinline__ void store_chunk_packed(OutT* out, int64_t ldo, int row0, int M, int col0, int N,
+                                                   const uint32_t* w, uint8_t* buf, int lane, bool vec_ok,
+                                                   bool evict_first) {
+  static_assert(sizeof(OutT) == 2, "packed stores are for 16-bit outputs");
+  if (!vec_ok || col0 + 32 > N) {
+    if (row0 + lane < M) {
+      unsigned short* dst = reinterpret_cast<unsigned short*>(out + (int64_t)(row0 + lane) * ldo + col0);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        if (col0 + 2 * j < N) dst[2 * j] = (unsigned short)(w[j] & 0xffffu);
+        if (col0 + 2 * j + 1 < N) dst[2 * j + 1] = (unsigned short)(w[j] >> 16);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int pc = 0; pc < 4; ++pc)
+    *reinterpret_cast<uint4*>(buf + lane * 64 + 16 * (pc ^ ((lane >> 1) & 3))) =
+        make_uint4(w[4 * pc], w[4 * pc + 1], w[4 * pc + 2], w[4 * pc + 3]);
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int r = j * 8 + (lane >> 2), pc = lane & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 64 + 16 * (pc ^ ((r >> 1) & 3)));
+    if (row0 + r < M) {
+      OutT* dst = out + (int64_t)(row0 + r) * ldo + col0 + pc * 8;
+      if (evict_first) st16_cs(dst, v);
+      else st16(dst, v);
+    }
+  }
+  __syncwarp();
+}
+
+// Fold 32 packed 16-bit logits (columns c * 32 .. c * 32 + 31 of a 256-column
+// half starting at n0) into the running (max, sum-exp) pair in log2 units,
+// and record the target logit if it lies in this chunk. Two 16-column
+// sub-chunks keep few values live.
+template <typename OutT>
+__device__ __forceinline__ void lce_fold_chunk(const uint32_t* w, int c, int n0, int N, int64_t lab_rel,
+                                               float* xt_row, float& m_run, float& s_run) {
+#pragma unroll
+  for (int sc = 0; sc < 2; ++sc) {
+    const int cs = n0 + c * 32 + sc * 16;
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) unpack2<OutT>(w[sc * 8 + j], x[2 * j], x[2 * j + 1]);
+    float cm = kNegInf;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (cs + j < N) cm = fmaxf(cm, x[j]);
+      if ((int64_t)(c * 32 + sc * 16 + j) == lab_rel) *xt_row = x[j];
+    }
+    const float mnew = fmaxf(m_run, cm * kLog2e);
+    float acc_s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (cs + j < N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
+    s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
+    m_run = mnew;
+  }
+}
+
 // Geometry of one configuration. PAIR = 1: one CTA computes a 128 x 256 tile.
 // PAIR = 2: a 2-CTA cluster computes a 256 x 256 tile with tcgen05.mma
 // cta_group::2; each CTA stages its 128 rows of A and 128 of the 256 B rows,
 // and holds its 128 accumulator rows in its own TMEM.
-template <int PAIR>
+// NSUB = 2 (pairs only): the pair tile is 256 x 512, two N = 256 MMAs per K
+// step share each staged A tile, so a CTA moves 48 KB from L2 per 8.4 MFLOP
+// instead of 32 KB per 4.2 MFLOP. Operand traffic from L2 is about a quarter
+// of the GEMM's energy and the GEMM runs at the power cap, so the wider tile
+// buys clock. The 128 x 512 fp32 accumulator fills all of TMEM, so the
+// halves are published and released separately: a tile's last STG k-steps
+// finish half 0 first (the epilogue drains it while half 1 finishes) and the
+// next tile's first STG k-steps run on half 0 while half 1 is drained.
+template <int PAIR, int NSUB = 1>
 struct Geo {
+  static_assert(NSUB == 1 || PAIR == 2, "the 512-column tile needs a CTA pair");
   static constexpr int TM = BM * PAIR;            // tile rows
-  static constexpr int B_ROWS = BN / PAIR;        // B rows staged per CTA
+  static constexpr int TN = BN * NSUB;            // tile columns
+  static constexpr int HB = BN / PAIR;            // B rows per CTA per 256-column half
+  static constexpr int B_ROWS = HB * NSUB;        // B rows staged per CTA
   static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int HALF_BYTES = HB * BK * 2;  // one half's B tile
   static constexpr int B_BYTES = B_ROWS * BK * 2;
-  static constexpr int STG = PAIR == 2 ? 6 : 4;   // pipeline depth
-  static constexpr int SMEM = STG * (A_BYTES + B_BYTES) + 1024 + 256;
+  static constexpr int STG = NSUB == 2 ? 4 : (PAIR == 2 ? 6 : 4);   // pipeline depth
+  // operand stages, 1 KB alignment slack, barriers (256 B), epilogue exchange
+  // (2 x 128 float2) and one 2 KB store-staging buffer per epilogue warp
+  static constexpr int SMEM = STG * (A_BYTES + B_BYTES) + 1024 + 256 + 2 * BM * 8 + EPI_WARPS * 2048;
 };
 
-template <typename T, int A_MN, int B_MN, int EPI, typename OutT, int PAIR>
+template <typename T, int A_MN, int B_MN, int EPI, typename OutT, int PAIR, int NSUB>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
-  using G = Geo<PAIR>;
+  using G = Geo<PAIR, NSUB>;
+  static_assert(NSUB == 1 || sizeof(OutT) == 2, "the 512-column tile parks 16-bit outputs only");
   constexpr int STG = G::STG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -173,11 +325,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* empty = full + STG;
   uint64_t* tfull = empty + STG;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* xready = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xready + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float2* xchg = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(full) + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  uint8_t* stage_out = reinterpret_cast<uint8_t*>(xchg + 2 * BM) + (warp >= EPI_WARP0 ? (warp - EPI_WARP0) * 2048 : 0);
   const uint32_t rank = PAIR == 2 ? tc::cluster_ctarank() : 0;
   const int unit = blockIdx.x / PAIR;         // cluster index
   const int nunits = gridDim.x / PAIR;
@@ -189,7 +344,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(&tfull[b], 1);
-      tc::mbar_init(&tempty[b], 4 * PAIR);
+      tc::mbar_init(&tempty[b], EPI_WARPS * PAIR);
+      tc::mbar_init(&xready[b], 4);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -219,7 +375,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         int mt, nt;
         tile_coords(p, tile, mt, nt);
         const int ma = mt * G::TM + (int)rank * BM;         // this CTA's A rows
-        const int nb = nt * BN + (int)rank * G::B_ROWS;     // this CTA's B rows
+        const int nb = nt * G::TN + (int)rank * G::HB;      // this CTA's B rows (first half)
         for (int kb = 0; kb < nkb; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, lim)) goto producer_done;
           uint8_t* a = sA + stage * G::A_BYTES;
@@ -250,12 +406,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             } else {
               tc::tma_load_2d_pair_hint(a, &tmA, fb, k0, ma, pol_a);
             }
-            if (B_MN) {
 #pragma unroll
-              for (int j = 0; j < G::B_ROWS / 64; ++j)
-                tc::tma_load_2d_pair_hint(b + j * (BK * 128), &tmB, fb, nb + j * 64, k0, pol_b);
-            } else {
-              tc::tma_load_2d_pair_hint(b, &tmB, fb, k0, nb, pol_b);
+            for (int h = 0; h < NSUB; ++h) {
+              uint8_t* bh = b + h * G::HALF_BYTES;
+              const int nbh = nb + h * BN;
+              if (B_MN) {
+#pragma unroll
+                for (int j = 0; j < G::HB / 64; ++j)
+                  tc::tma_load_2d_pair_hint(bh + j * (BK * 128), &tmB, fb, nbh + j * 64, k0, pol_b);
+              } else {
+                tc::tma_load_2d_pair_hint(bh, &tmB, fb, k0, nbh, pol_b);
+              }
             }
           }
           if (++stage == STG) { stage = 0; phase ^= 1; }
@@ -277,6 +438,75 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      if (NSUB == 2) {
+        // One 512-column accumulator: half h at columns [h * BN, h * BN + BN).
+        // The first `pre` k-steps run on half 0 only and keep their stages;
+        // once the epilogue has released half 1 they are replayed on it and
+        // freed, then both halves advance together.
+        auto issue = [&](int st_, int h, bool first) {
+          const uint32_t a0 = tc::smem_u32(sA + st_ * G::A_BYTES);
+          const uint32_t b0 = tc::smem_u32(sB + st_ * G::B_BYTES + h * G::HALF_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = tc::smem_desc_sw128(a0 + k * a_kstep, a_lbo, a_sbo);
+            const uint64_t bd = tc::smem_desc_sw128(b0 + k * b_kstep, b_lbo, b_sbo);
+            tc::mma_f16_pair(tmem_base + h * BN, ad, bd, idesc, !(first && k == 0));
+          }
+        };
+        // k-steps [0, pre) open a tile on half 0 while the epilogue still
+        // drains half 1 of the previous tile; k-steps [nkb - tail, nkb) close
+        // it half 0 first, so the epilogue starts on half 0 while the tensor
+        // pipe finishes half 1.
+        const int pre = nkb < STG ? nkb : STG;
+        const int tail = nkb - pre < STG ? nkb - pre : STG;
+        for (int tile = unit; tile < p.num_tiles; tile += nunits) {
+          if (!tc::mbar_wait(&tempty[0], acc_phase ^ 1, abort_flag, lim)) break;
+          tc::tc_fence_after();
+          bool ok = true;
+          int s = stage;
+          uint32_t ph = phase;
+          for (int kb = 0; kb < pre; ++kb) {
+            if (!tc::mbar_wait(&full[s], ph, abort_flag, lim)) { ok = false; break; }
+            tc::tc_fence_after();
+            issue(s, 0, kb == 0);
+            if (++s == STG) { s = 0; ph ^= 1; }
+          }
+          if (!ok) break;
+          if (!tc::mbar_wait(&tempty[1], acc_phase ^ 1, abort_flag, lim)) break;
+          tc::tc_fence_after();
+          for (int kb = 0; kb < pre; ++kb) {
+            issue(stage, 1, kb == 0);
+            tc::mma_commit_pair_mc(&empty[stage], 0x3);
+            if (++stage == STG) { stage = 0; phase ^= 1; }
+          }
+          for (int kb = pre; kb < nkb - tail; ++kb) {
+            if (!tc::mbar_wait(&full[stage], phase, abort_flag, lim)) { ok = false; break; }
+            tc::tc_fence_after();
+            issue(stage, 0, false);
+            issue(stage, 1, false);
+            tc::mma_commit_pair_mc(&empty[stage], 0x3);
+            if (++stage == STG) { stage = 0; phase ^= 1; }
+          }
+          if (!ok) break;
+          s = stage;
+          ph = phase;
+          for (int kb = 0; kb < tail; ++kb) {
+            if (!tc::mbar_wait(&full[s], ph, abort_flag, lim)) { ok = false; break; }
+            tc::tc_fence_after();
+            issue(s, 0, false);
+            if (++s == STG) { s = 0; ph ^= 1; }
+          }
+          if (!ok) break;
+          tc::mma_commit_pair_mc(&tfull[0], 0x3);
+          for (int kb = 0; kb < tail; ++kb) {
+            issue(stage, 1, false);
+            tc::mma_commit_pair_mc(&empty[stage], 0x3);
+            if (++stage == STG) { stage = 0; phase ^= 1; }
+          }
+          tc::mma_commit_pair_mc(&tfull[1], 0x3);
+          acc_phase ^= 1;
+        }
+      } else
       for (int tile = unit; tile < p.num_tiles; tile += nunits) {
         if (!tc::mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, lim)) break;
         tc::tc_fence_after();
@@ -304,93 +534,220 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp >= EPI_WARP0) {
     // ---------------- epilogue ----------------
-    const int q = warp - 4;  // TMEM lane quarter this warp may access
+    // Two groups of four warps; warp w reads TMEM lanes 32 * (w % 4) and group
+    // g takes columns [g * 128, g * 128 + 128) of each 256-column half. TMEM
+    // loads run one 32-column chunk ahead of the math.
+    const int q = warp & 3;
+    const int g = (warp - EPI_WARP0) >> 2;
     const uint32_t tempty_leader0 = tc::mapa_shared(tc::smem_u32(&tempty[0]), 0);
     const uint32_t tempty_leader1 = tc::mapa_shared(tc::smem_u32(&tempty[1]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = unit; tile < p.num_tiles; tile += nunits) {
+    int xbuf = 0;
+    uint32_t xphase = 0;  // bit b: phase of xready[b]
+    bool stop = false;
+    for (int tile = unit; tile < p.num_tiles && !stop; tile += nunits) {
       int mt, nt;
       tile_coords(p, tile, mt, nt);
-      const int m0 = mt * G::TM + (int)rank * BM, n0 = nt * BN;
-      if (!tc::mbar_wait(&tfull[acc], acc_phase, abort_flag, lim)) break;
-      tc::tc_fence_after();
+      const int m0 = mt * G::TM + (int)rank * BM;
+      if (NSUB == 1) {
+        if (!tc::mbar_wait(&tfull[acc], acc_phase, abort_flag, lim)) break;
+        tc::tc_fence_after();
+      }
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      if (EPI == EPI_LCE) {
-        const int64_t lab = row_ok ? p.labels[row] - p.label_offset : -1;
-        const int64_t lab_rel = lab - n0;  // label column inside this tile, if any
-        float m_run = kNegInf, s_run = 0.f;
-        OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)row * p.ldo;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          __syncwarp();
-          tc::tmem_ld32(tbase + c * 32, r);
-          tc::tmem_ld_wait();
-          float x[32];
-          float cm = kNegInf;
-          const int col0 = n0 + c * 32;
+      if constexpr (NSUB == 2) {
+        {
+          // 512-column tile, 16-bit output. Each warp drains its 4 chunks of a
+          // half from TMEM, finishes the first at once and parks the other 3
+          // as packed 16-bit values in registers, then releases the half: the
+          // MMAs get TMEM back after ~1/4 of the epilogue work. The parked
+          // chunks (CE statistics and the stores, whose shared-memory traffic
+          // competes with the MMAs' operand reads) are done afterwards while
+          // the next tile's MMAs run.
+          constexpr int PW = (EPI_CHUNKS - 1) * 16;  // parked words per half
+          uint32_t pk[2][PW];
+          float hm[2] = {kNegInf, kNegInf}, hs[2] = {0.f, 0.f};
+          const float scale = (EPI == EPI_STORE && p.scale) ? *p.scale : 1.f;
+          const int64_t lab = (EPI == EPI_LCE && row_ok) ? p.labels[row] - p.label_offset : -1;
+          float* xt_row = EPI == EPI_LCE ? p.xt + row : nullptr;
+          OutT* out = reinterpret_cast<OutT*>(p.out);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            // the logits tensor holds the product rounded to the input dtype
-            // (as the reference's cuBLAS output); statistics use those values
-            x[j] = Elt<OutT>::to_f(Elt<OutT>::from_f(__uint_as_float(r[j])));
-            if (col0 + j < p.N) cm = fmaxf(cm, x[j]);
-            if ((int64_t)(c * 32 + j) == lab_rel) p.xt[row] = x[j];
-          }
-          const float cm2 = cm * kLog2e;
-          const float mnew = fmaxf(m_run, cm2);
-          float acc_s = 0.f;
+          for (int h = 0; h < 2; ++h) {
+            if (!tc::mbar_wait(&tfull[h], acc_phase, abort_flag, lim)) { stop = true; break; }
+            tc::tc_fence_after();
+            const int n0 = nt * G::TN + h * BN;
+            if (n0 < p.N) {
+              const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + h * BN + g * EPI_CHUNKS * 32;
+              __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
-          s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
-          m_run = mnew;
-          if (row_ok && p.out) store_row32<OutT>(orow, col0, p.N, x, p.vec_ok, p.out_evict_first);
-        }
-        if (row_ok) p.stats[(int64_t)nt * p.M + row] = make_float2(m_run, s_run);
-      } else {
-        const float scale = p.scale ? *p.scale : 1.f;
-        OutT* orow = reinterpret_cast<OutT*>(p.out) + (int64_t)row * p.ldo;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          __syncwarp();
-          tc::tmem_ld32(tbase + c * 32, r);
-          tc::tmem_ld_wait();
-          const int col0 = n0 + c * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
+              for (int i = 0; i < EPI_CHUNKS; ++i) {
+                uint32_t w[16];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
-            if (p.add_f32) {
-              float a[32];
-              load_row32<float>(p.add_f32 + (int64_t)row * p.ldadd, col0, p.N, a, p.vec_ok);
+                for (int sc = 0; sc < 2; ++sc) {
+                  uint32_t r[16];
+                  tc::tmem_ld16_wait(tb + i * 32 + sc * 16, r);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += a[j];
-            } else if (p.add_same) {
-              float a[32];
-              load_row32<OutT>(reinterpret_cast<const OutT*>(p.add_same) + (int64_t)row * p.ldadd, col0, p.N, a,
-                               p.vec_ok);
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] += a[j];
+                  for (int j = 0; j < 8; ++j) {
+                    const uint32_t v =
+                        pack2<OutT>(__uint_as_float(r[2 * j]) * scale, __uint_as_float(r[2 * j + 1]) * scale);
+                    if (i == 0) w[sc * 8 + j] = v;
+                    else pk[h][(i - 1) * 16 + sc * 8 + j] = v;
+                  }
+                }
+                if (i == 0) {
+                  const int c = g * EPI_CHUNKS;
+                  if (EPI == EPI_LCE) lce_fold_chunk<OutT>(w, c, n0, p.N, lab - n0, xt_row, hm[h], hs[h]);
+                  if (out)
+                    store_chunk_packed<OutT>(out, p.ldo, m0 + q * 32, p.M, n0 + c * 32, p.N, w, stage_out, lane,
+                                             p.vec_ok, p.out_evict_first);
+                }
+              }
             }
-            store_row32<OutT>(orow, col0, p.N, v, p.vec_ok, p.out_evict_first);
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive_cluster(h ? tempty_leader1 : tempty_leader0);
+          }
+          if (stop) break;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int n0 = nt * G::TN + h * BN;
+            if (n0 >= p.N) continue;
+#pragma unroll
+            for (int i = 1; i < EPI_CHUNKS; ++i) {
+              const int c = g * EPI_CHUNKS + i;
+              if (EPI == EPI_LCE) lce_fold_chunk<OutT>(&pk[h][(i - 1) * 16], c, n0, p.N, lab - n0, xt_row, hm[h], hs[h]);
+              if (out)
+                store_chunk_packed<OutT>(out, p.ldo, m0 + q * 32, p.M, n0 + c * 32, p.N, &pk[h][(i - 1) * 16],
+                                         stage_out, lane, p.vec_ok, p.out_evict_first);
+            }
+            if (EPI == EPI_LCE) {
+              // group 1 hands its (max, sum) to group 0, which writes the half's stats
+              float2* xs = xchg + xbuf * BM;
+              if (g == 1) {
+                xs[q * 32 + lane] = make_float2(hm[h], hs[h]);
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&xready[xbuf]);
+              } else if (tc::mbar_wait(&xready[xbuf], (xphase >> xbuf) & 1u, abort_flag, lim)) {
+                const float2 o = xs[q * 32 + lane];
+                const MS t = ms_merge(MS{hm[h], hs[h]}, MS{o.x, o.y});
+                if (row_ok) p.stats[(int64_t)(nt * NSUB + h) * p.M + row] = make_float2(t.m, t.s);
+              } else {
+                stop = true;
+              }
+              xphase ^= 1u << xbuf;
+              xbuf ^= 1;
+            }
+          }
+          acc_phase ^= 1;
+        }
+      } else {
+#pragma unroll 1
+      for (int h = 0; h < NSUB; ++h) {
+        if (NSUB == 2) {  // each half is published on its own barrier
+          if (!tc::mbar_wait(&tfull[h], acc_phase, abort_flag, lim)) { stop = true; break; }
+          tc::tc_fence_after();
+        }
+        const int n0 = nt * G::TN + h * BN;
+        const int sub = NSUB == 2 ? h : acc;  // accumulator (half) index
+        const int c0 = g * EPI_CHUNKS;        // first 32-column chunk of this group
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + sub * BN + c0 * 32;
+        if (n0 < p.N) {
+          uint32_t ra[32], rb[32];
+          __syncwarp();
+          tc::tmem_ld32(tbase, ra);
+          if (EPI == EPI_LCE) {
+            const int64_t lab = row_ok ? p.labels[row] - p.label_offset : -1;
+            const int64_t lab_rel = lab - n0;  // label column inside this half, if any
+            float m_run = kNegInf, s_run = 0.f;
+#pragma unroll
+            for (int i = 0; i < EPI_CHUNKS; ++i) {
+              uint32_t(&r)[32] = (i & 1) ? rb : ra;
+              tc::tmem_ld_wait(r);
+              if (i + 1 < EPI_CHUNKS) tc::tmem_ld32(tbase + (i + 1) * 32, (i & 1) ? ra : rb);
+              const int c = c0 + i;
+              float x[32];
+              float cm = kNegInf;
+              const int col0 = n0 + c * 32;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                // the logits tensor holds the product rounded to the input dtype
+                // (as the reference's cuBLAS output); statistics use those values
+                x[j] = Elt<OutT>::to_f(Elt<OutT>::from_f(__uint_as_float(r[j])));
+                if (col0 + j < p.N) cm = fmaxf(cm, x[j]);
+                if ((int64_t)(c * 32 + j) == lab_rel) p.xt[row] = x[j];
+              }
+              const float cm2 = cm * kLog2e;
+              const float mnew = fmaxf(m_run, cm2);
+              float acc_s = 0.f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
+              s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
+              m_run = mnew;
+              if (p.out)
+                store_chunk<OutT>(reinterpret_cast<OutT*>(p.out), p.ldo, m0 + q * 32, p.M, col0, p.N, x, stage_out,
+                                  lane, p.vec_ok, p.out_evict_first);
+            }
+            // group 1 hands its (max, sum) to group 0, which writes the half's stats
+            float2* xs = xchg + xbuf * BM;
+            if (g == 1) {
+              xs[q * 32 + lane] = make_float2(m_run, s_run);
+              __syncwarp();
+              if (lane == 0) tc::mbar_arrive(&xready[xbuf]);
+            } else if (tc::mbar_wait(&xready[xbuf], (xphase >> xbuf) & 1u, abort_flag, lim)) {
+              const float2 o = xs[q * 32 + lane];
+              const MS t = ms_merge(MS{m_run, s_run}, MS{o.x, o.y});
+              if (row_ok) p.stats[(int64_t)(nt * NSUB + h) * p.M + row] = make_float2(t.m, t.s);
+            } else {
+              stop = true;
+            }
+            xphase ^= 1u << xbuf;
+            xbuf ^= 1;
+          } else {
+            const float scale = p.scale ? *p.scale : 1.f;
+#pragma unroll
+            for (int i = 0; i < EPI_CHUNKS; ++i) {
+              uint32_t(&r)[32] = (i & 1) ? rb : ra;
+              tc::tmem_ld_wait(r);
+              if (i + 1 < EPI_CHUNKS) tc::tmem_ld32(tbase + (i + 1) * 32, (i & 1) ? ra : rb);
+              const int col0 = n0 + (c0 + i) * 32;
+              if (col0 < p.N) {
+                float v[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * scale;
+                if (!row_ok) {
+                } else if (p.add_f32) {
+                  float a[32];
+                  load_row32<float>(p.add_f32 + (int64_t)row * p.ldadd, col0, p.N, a, p.vec_ok);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += a[j];
+                } else if (p.add_same) {
+                  float a[32];
+                  load_row32<OutT>(reinterpret_cast<const OutT*>(p.add_same) + (int64_t)row * p.ldadd, col0, p.N,
+                                   a, p.vec_ok);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += a[j];
+                }
+                store_chunk<OutT>(reinterpret_cast<OutT*>(p.out), p.ldo, m0 + q * 32, p.M, col0, p.N, v, stage_out,
+                                  lane, p.vec_ok, p.out_evict_first);
+              }
+            }
           }
         }
-      }
-      // release this accumulator buffer to the (leader's) MMA warp
-      tc::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (PAIR == 2) tc::mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
-        else tc::mbar_arrive(&tempty[acc]);
+        // release this accumulator buffer (half) to the (leader's) MMA warp
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (PAIR == 2) tc::mbar_arrive_cluster(sub ? tempty_leader1 : tempty_leader0);
+          else tc::mbar_arrive(&tempty[sub]);
+        }
+        if (stop) break;
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
     }
   }
   __syncthreads();
