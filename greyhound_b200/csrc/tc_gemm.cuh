@@ -254,32 +254,71 @@ __device__ __forceinline__ void store_chunk_packed(OutT* out, int64_t ldo, int r
   __syncwarp();
 }
 
+// Fold 16 logits starting at column cs into the running (max, sum-exp) pair
+// in log2 units. `full`: all 16 columns are < N (the common case: no
+// per-element predicates).
+__device__ __forceinline__ void lce_fold16(const float (&x)[16], bool full, int cs, int N, float& m_run, float& s_run) {
+  float cm;
+  if (full) {
+    float t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = fmaxf(x[2 * j], x[2 * j + 1]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = fmaxf(t[2 * j], t[2 * j + 1]);
+    cm = fmaxf(fmaxf(t[0], t[1]), fmaxf(t[2], t[3]));
+  } else {
+    cm = kNegInf;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (cs + j < N) cm = fmaxf(cm, x[j]);
+  }
+  const float mnew = fmaxf(m_run, cm * kLog2e);
+  float a0 = 0.f, a1 = 0.f;
+  if (full) {
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      a0 += fast_exp2(fmaf(x[j], kLog2e, -mnew));
+      a1 += fast_exp2(fmaf(x[j + 1], kLog2e, -mnew));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (cs + j < N) a0 += fast_exp2(fmaf(x[j], kLog2e, -mnew));
+  }
+  s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + (a0 + a1);
+  m_run = mnew;
+}
+
 // Fold 32 packed 16-bit logits (columns c * 32 .. c * 32 + 31 of a 256-column
-// half starting at n0) into the running (max, sum-exp) pair in log2 units,
-// and record the target logit if it lies in this chunk. Two 16-column
-// sub-chunks keep few values live.
+// half starting at n0) into the running pair and record the target logit if
+// it lies in this chunk (lab_rel: target column relative to n0). Two
+// 16-column sub-chunks keep few values live.
 template <typename OutT>
 __device__ __forceinline__ void lce_fold_chunk(const uint32_t* w, int c, int n0, int N, int64_t lab_rel,
                                                float* xt_row, float& m_run, float& s_run) {
+  const int col0 = n0 + c * 32;
+  const bool full = col0 + 32 <= N;
 #pragma unroll
   for (int sc = 0; sc < 2; ++sc) {
-    const int cs = n0 + c * 32 + sc * 16;
     float x[16];
 #pragma unroll
     for (int j = 0; j < 8; ++j) unpack2<OutT>(w[sc * 8 + j], x[2 * j], x[2 * j + 1]);
-    float cm = kNegInf;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if (cs + j < N) cm = fmaxf(cm, x[j]);
-      if ((int64_t)(c * 32 + sc * 16 + j) == lab_rel) *xt_row = x[j];
-    }
-    const float mnew = fmaxf(m_run, cm * kLog2e);
-    float acc_s = 0.f;
+    lce_fold16(x, full, col0 + sc * 16, N, m_run, s_run);
+  }
+  const int64_t li = lab_rel - c * 32;
+  if ((uint64_t)li < 32u) {
+    // one select per word, written so the compiler cannot turn the chain
+    // into an indexed load (that would move w to local memory)
+    uint32_t word = 0;
+    const int wi = (int)(li >> 1);
 #pragma unroll
     for (int j = 0; j < 16; ++j)
-      if (cs + j < N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
-    s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
-    m_run = mnew;
+      asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\tselp.b32 %0, %1, %0, p;\n\t}"
+          : "+r"(word)
+          : "r"(w[j]), "r"(wi), "r"(j));
+    float lo, hi;
+    unpack2<OutT>(word, lo, hi);
+    *xt_row = (li & 1) ? hi : lo;
   }
 }
 
@@ -655,41 +694,29 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int c0 = g * EPI_CHUNKS;        // first 32-column chunk of this group
         const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + sub * BN + c0 * 32;
         if (n0 < p.N) {
-          uint32_t ra[32], rb[32];
           __syncwarp();
-          tc::tmem_ld32(tbase, ra);
-          if (EPI == EPI_LCE) {
+          if constexpr (EPI == EPI_LCE) {
             const int64_t lab = row_ok ? p.labels[row] - p.label_offset : -1;
             const int64_t lab_rel = lab - n0;  // label column inside this half, if any
             float m_run = kNegInf, s_run = 0.f;
-#pragma unroll
+#pragma unroll 1
             for (int i = 0; i < EPI_CHUNKS; ++i) {
-              uint32_t(&r)[32] = (i & 1) ? rb : ra;
-              tc::tmem_ld_wait(r);
-              if (i + 1 < EPI_CHUNKS) tc::tmem_ld32(tbase + (i + 1) * 32, (i & 1) ? ra : rb);
               const int c = c0 + i;
-              float x[32];
-              float cm = kNegInf;
-              const int col0 = n0 + c * 32;
+              // the logits tensor holds the product rounded to the input dtype
+              // (as the reference's cuBLAS output); statistics use those values
+              uint32_t w[16];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                // the logits tensor holds the product rounded to the input dtype
-                // (as the reference's cuBLAS output); statistics use those values
-                x[j] = Elt<OutT>::to_f(Elt<OutT>::from_f(__uint_as_float(r[j])));
-                if (col0 + j < p.N) cm = fmaxf(cm, x[j]);
-                if ((int64_t)(c * 32 + j) == lab_rel) p.xt[row] = x[j];
+              for (int sc = 0; sc < 2; ++sc) {
+                uint32_t r[16];
+                tc::tmem_ld16_wait(tbase + i * 32 + sc * 16, r);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  w[sc * 8 + j] = pack2<OutT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
               }
-              const float cm2 = cm * kLog2e;
-              const float mnew = fmaxf(m_run, cm2);
-              float acc_s = 0.f;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) acc_s += fast_exp2(fmaf(x[j], kLog2e, -mnew));
-              s_run = (m_run == kNegInf ? 0.f : s_run * fast_exp2(m_run - mnew)) + acc_s;
-              m_run = mnew;
+              lce_fold_chunk<OutT>(w, c, n0, p.N, lab_rel, p.xt + row, m_run, s_run);
               if (p.out)
-                store_chunk<OutT>(reinterpret_cast<OutT*>(p.out), p.ldo, m0 + q * 32, p.M, col0, p.N, x, stage_out,
-                                  lane, p.vec_ok, p.out_evict_first);
+                store_chunk_packed<OutT>(reinterpret_cast<OutT*>(p.out), p.ldo, m0 + q * 32, p.M, n0 + c * 32, p.N, w,
+                                         stage_out, lane, p.vec_ok, p.out_evict_first);
             }
             // group 1 hands its (max, sum) to group 0, which writes the half's stats
             float2* xs = xchg + xbuf * BM;
@@ -708,6 +735,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             xbuf ^= 1;
           } else {
             const float scale = p.scale ? *p.scale : 1.f;
+            uint32_t ra[32], rb[32];
+            tc::tmem_ld32(tbase, ra);
 #pragma unroll
             for (int i = 0; i < EPI_CHUNKS; ++i) {
               uint32_t(&r)[32] = (i & 1) ? rb : ra;
