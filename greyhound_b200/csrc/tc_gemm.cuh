@@ -364,8 +364,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint64_t* empty = full + STG;
   uint64_t* tfull = empty + STG;
   uint64_t* tempty = tfull + 2;
-  uint64_t* xready = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xready + 2);
+  uint64_t* xready = tempty + 2;  // group 1's (max, sum) of a half is in xchg[b]
+  uint64_t* xdone = xready + 2;   // group 0 has read xchg[b]
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(xdone + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float2* xchg = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(full) + 256);
 
@@ -385,6 +386,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc::mbar_init(&tfull[b], 1);
       tc::mbar_init(&tempty[b], EPI_WARPS * PAIR);
       tc::mbar_init(&xready[b], 4);
+      tc::mbar_init(&xdone[b], 4);
     }
     *abort_flag = 0;
     tc::fence_barrier_init();
@@ -597,6 +599,31 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < p.M;
+      // Both groups hold (max, sum) partials of the same rows for one
+      // 256-column block; group 1 hands its pair to group 0 through
+      // xchg[xbuf], and group 0 writes the merged statistics of block `sub`.
+      // xready / xdone order the two sides of each buffer's every use.
+      auto stats_exchange_at = [&](int sub, float m, float sm) -> bool {
+        float2* xs = xchg + xbuf * BM;
+        const uint32_t ph = (xphase >> xbuf) & 1u;
+        bool ok = true;
+        if (g == 1) {
+          if ((ok = tc::mbar_wait(&xdone[xbuf], ph ^ 1u, abort_flag, lim))) {
+            xs[q * 32 + lane] = make_float2(m, sm);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&xready[xbuf]);
+          }
+        } else if ((ok = tc::mbar_wait(&xready[xbuf], ph, abort_flag, lim))) {
+          const float2 o = xs[q * 32 + lane];
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&xdone[xbuf]);
+          const MS t = ms_merge(MS{m, sm}, MS{o.x, o.y});
+          if (row_ok) p.stats[(int64_t)(nt * NSUB + sub) * p.M + row] = make_float2(t.m, t.s);
+        }
+        xphase ^= 1u << xbuf;
+        xbuf ^= 1;
+        return ok;
+      };
       if constexpr (NSUB == 2) {
         {
           // 512-column tile, 16-bit output. Each warp drains its 4 chunks of a
@@ -664,20 +691,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
             if (EPI == EPI_LCE) {
               // group 1 hands its (max, sum) to group 0, which writes the half's stats
-              float2* xs = xchg + xbuf * BM;
-              if (g == 1) {
-                xs[q * 32 + lane] = make_float2(hm[h], hs[h]);
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&xready[xbuf]);
-              } else if (tc::mbar_wait(&xready[xbuf], (xphase >> xbuf) & 1u, abort_flag, lim)) {
-                const float2 o = xs[q * 32 + lane];
-                const MS t = ms_merge(MS{hm[h], hs[h]}, MS{o.x, o.y});
-                if (row_ok) p.stats[(int64_t)(nt * NSUB + h) * p.M + row] = make_float2(t.m, t.s);
-              } else {
-                stop = true;
-              }
-              xphase ^= 1u << xbuf;
-              xbuf ^= 1;
+              if (!stats_exchange_at(h, hm[h], hs[h])) stop = true;
             }
           }
           acc_phase ^= 1;
@@ -719,20 +733,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                                          stage_out, lane, p.vec_ok, p.out_evict_first);
             }
             // group 1 hands its (max, sum) to group 0, which writes the half's stats
-            float2* xs = xchg + xbuf * BM;
-            if (g == 1) {
-              xs[q * 32 + lane] = make_float2(m_run, s_run);
-              __syncwarp();
-              if (lane == 0) tc::mbar_arrive(&xready[xbuf]);
-            } else if (tc::mbar_wait(&xready[xbuf], (xphase >> xbuf) & 1u, abort_flag, lim)) {
-              const float2 o = xs[q * 32 + lane];
-              const MS t = ms_merge(MS{m_run, s_run}, MS{o.x, o.y});
-              if (row_ok) p.stats[(int64_t)(nt * NSUB + h) * p.M + row] = make_float2(t.m, t.s);
-            } else {
-              stop = true;
-            }
-            xphase ^= 1u << xbuf;
-            xbuf ^= 1;
+            if (!stats_exchange_at(h, m_run, s_run)) stop = true;
           } else {
             const float scale = p.scale ? *p.scale : 1.f;
             uint32_t ra[32], rb[32];
