@@ -578,8 +578,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else if (warp >= EPI_WARP0) {
     // ---------------- epilogue ----------------
     // Two groups of four warps; warp w reads TMEM lanes 32 * (w % 4) and group
-    // g takes columns [g * 128, g * 128 + 128) of each 256-column half. TMEM
-    // loads run one 32-column chunk ahead of the math.
+    // g takes columns [g * 128, g * 128 + 128) of each 256-column block. In
+    // the plain-store path TMEM loads run one 32-column chunk ahead of the
+    // math; the CE paths load 16 columns at a time to stay within registers.
     const int q = warp & 3;
     const int g = (warp - EPI_WARP0) >> 2;
     const uint32_t tempty_leader0 = tc::mapa_shared(tc::smem_u32(&tempty[0]), 0);
