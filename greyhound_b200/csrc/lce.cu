@@ -186,19 +186,46 @@ inline int wide_mode() {
   }();
   return mode;
 }
-inline int pick_nsub(int64_t M, int64_t N, int pair, int units, bool fp32_epilogue, bool lce_epilogue) {
-  if (pair != 2 || N <= BN || fp32_epilogue) return 1;
+// Tiling of one GEMM: tile width (nsub) and split-K slices (ksplit).
+struct Tiling {
+  int nsub = 1, ksplit = 1;
+};
+// Split-K (2 slices, 512-column tiles; the slices write two 16-bit partials
+// that a small kernel adds) when the caller provides the second output and
+// the unsplit wide tiles would leave a short last wave: dH at the Llama-3-8B
+// head (8192 x 4096 output) has 256 wide tiles for 74 pair units (a 46 %
+// last wave) but 512 split units (6.9 full waves). Charged 1 % for the add.
+inline Tiling pick_tiling(int64_t M, int64_t N, int64_t K, int pair, int units, bool fp32_epilogue,
+                          bool lce_epilogue, bool split_ok = false) {
+  Tiling t;
+  if (pair != 2 || N <= BN || fp32_epilogue) return t;
   const int mode = wide_mode();
-  if (mode != 1) return mode == 2 ? 2 : 1;
-  if (lce_epilogue) return 1;
-  auto eff = [&](int64_t tn) {
-    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + tn - 1) / tn);
+  if (mode != 1) {
+    t.nsub = mode == 2 ? 2 : 1;
+    return t;
+  }
+  if (lce_epilogue) return t;
+  auto eff = [&](int64_t tn, int64_t ks) {
+    const int64_t tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + tn - 1) / tn) * ks;
     const int64_t waves = (tiles + units - 1) / units;
     // useful columns per computed column (a partial last tile computes zeros)
     const double fill = (double)N / (double)(((N + tn - 1) / tn) * tn);
     return (double)tiles / (double)(waves * units) * fill;
   };
-  return eff(2 * BN) * 1.06 >= eff(BN) ? 2 : 1;
+  const double narrow = eff(BN, 1), wide = eff(2 * BN, 1) * 1.06;
+  // each slice keeps at least 4 stage rounds of k-steps
+  const bool can_split = split_ok && (K + BK - 1) / BK >= 2 * 16;
+  const double wide_split = can_split ? eff(2 * BN, 2) * 1.06 * 0.99 : 0.0;
+  if (wide_split > wide * 1.02 && wide_split > narrow) {
+    t.nsub = 2;
+    t.ksplit = 2;
+  } else if (wide >= narrow) {
+    t.nsub = 2;
+  }
+  return t;
+}
+inline int pick_nsub(int64_t M, int64_t N, int pair, int units, bool fp32_epilogue, bool lce_epilogue) {
+  return pick_tiling(M, N, 0, pair, units, fp32_epilogue, lce_epilogue).nsub;
 }
 
 // Tensor maps of both operands for a GEMM of M x N x K with pairing `pair`.
@@ -213,13 +240,14 @@ int make_operand_maps(CUtensorMap* ta, CUtensorMap* tb, int dtype, const Operand
   return rc;
 }
 
-void set_tiles(gemm::Params& p, int64_t M, int64_t N, int64_t K, int pair, int nsub = 1) {
+void set_tiles(gemm::Params& p, int64_t M, int64_t N, int64_t K, int pair, int nsub = 1, int ksplit = 1) {
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
   p.num_m = (int)((M + BM * pair - 1) / (BM * pair));
   p.num_n = (int)((N + BN * nsub - 1) / (BN * nsub));
-  p.num_tiles = p.num_m * p.num_n;
+  p.ksplit = ksplit;
+  p.num_tiles = p.num_m * p.num_n * ksplit;
 }
 
 // Generic: D[M,N] = scale * A B^T (+ addend), D written as out_dtype with pitch ldo.
@@ -240,10 +268,48 @@ constexpr int kLogitsGroup = 16;
 constexpr Hints kStreamA_KeepB{1, 2, 1};
 constexpr Hints kKeepA_StreamB{2, 1, 1};
 
+// out[r, c] = out[r, c] + part[r, c] (16-bit, fp32 add, one rounding) over
+// rows of pitch ld: the second split-K slice folded into the first.
+template <typename T>
+__global__ void __launch_bounds__(256) add_partial_kernel(T* out, const T* __restrict__ part, int64_t rows,
+                                                          int64_t cols, int64_t ld) {
+  constexpr int PER = 16 / sizeof(T);
+  const int64_t vpr = cols / PER;  // whole vectors per row (rows are 16-byte aligned)
+  const int64_t nvec = rows * vpr;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    const int64_t r = i / vpr, c = (i - r * vpr) * PER;
+    Vec16<T> a, b;
+    a.raw = *reinterpret_cast<const uint4*>(out + r * ld + c);
+    b.raw = ld16_last(part + r * ld + c);
+    float fa[PER], fb[PER];
+    a.to_float(fa);
+    b.to_float(fb);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) fa[k] += fb[k];
+    a.from_float(fa);
+    st16(out + r * ld + c, a.raw);
+  }
+  const int64_t tail = cols - vpr * PER;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * tail; i += stride) {
+    const int64_t r = i / tail, c = vpr * PER + (i - r * tail);
+    out[r * ld + c] = Elt<T>::from_f(Elt<T>::to_f(out[r * ld + c]) + Elt<T>::to_f(part[r * ld + c]));
+  }
+}
+
+template <typename T>
+int add_partial(void* out, const void* part, int64_t rows, int64_t cols, int64_t ld, int max_ctas, cudaStream_t st) {
+  const int sms = num_sms_dev();
+  int grid = 4 * (max_ctas > 0 && max_ctas < sms ? max_ctas : sms);
+  add_partial_kernel<T><<<grid, 256, 0, st>>>(static_cast<T*>(out), static_cast<const T*>(part), rows, cols, ld);
+  count_launch(1);
+  return check_launch("add_partial");
+}
+
 int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N, int64_t K, void* out,
              int out_dtype, int64_t ldo, const float* add_f32, const void* add_same, int64_t ldadd,
              const float* scale, int raster, int max_ctas, cudaStream_t st, int* status,
-             int prof_class = PROF_GEMM_OTHER, Hints hints = Hints{}) {
+             int prof_class = PROF_GEMM_OTHER, Hints hints = Hints{}, void* split_out = nullptr) {
   if (M <= 0 || N <= 0) return GH_OK;
   if (K <= 0) return set_error(GH_EINVAL, "GEMM needs K >= 1");
   ProfScope prof(prof_class, st);
@@ -251,12 +317,17 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
   const int pair = pick_pair(M);
   int units = num_sms_dev() / 2;
   if (max_ctas > 0 && max_ctas / 2 < units) units = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
-  const int nsub = pick_nsub(M, N, pair, units, out_dtype == GH_F32 || add_f32 || add_same, false);
+  const bool split_ok = split_out && out_dtype != GH_F32 &&
+                        ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(split_out) |
+                          (uintptr_t)(ldo * elt_size(out_dtype))) & 15) == 0;
+  const Tiling tl = pick_tiling(M, N, K, pair, units, out_dtype == GH_F32 || add_f32 || add_same, false, split_ok);
+  const int nsub = tl.nsub;
   CUtensorMap ta, tb;
   int rc = make_operand_maps(&ta, &tb, dtype, A, B, M, N, K, pair);
   if (rc) return rc;
   gemm::Params p{};
-  set_tiles(p, M, N, K, pair, nsub);
+  set_tiles(p, M, N, K, pair, nsub, tl.ksplit);
+  p.out2 = tl.ksplit > 1 ? split_out : nullptr;
   p.raster = raster;
   p.group = 1;
   p.out = out;
@@ -275,10 +346,16 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
   p.out_evict_first = hints.out;
   if (dtype == GH_BF16) {
     if (out_dtype == GH_F32) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
-    if (out_dtype == GH_BF16) return launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
+    if (out_dtype == GH_BF16) {
+      rc = launch_gemm_mm<__nv_bfloat16, gemm::EPI_STORE, __nv_bfloat16>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
+      return rc || tl.ksplit == 1 ? rc : add_partial<__nv_bfloat16>(out, split_out, M, N, ldo, max_ctas, st);
+    }
   } else if (dtype == GH_F16) {
     if (out_dtype == GH_F32) return launch_gemm_mm<__half, gemm::EPI_STORE, float>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
-    if (out_dtype == GH_F16) return launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
+    if (out_dtype == GH_F16) {
+      rc = launch_gemm_mm<__half, gemm::EPI_STORE, __half>(ta, tb, A.mn_major, B.mn_major, pair, nsub, p, max_ctas, st);
+      return rc || tl.ksplit == 1 ? rc : add_partial<__half>(out, split_out, M, N, ldo, max_ctas, st);
+    }
   }
   return set_error(GH_ETYPE, "unsupported GEMM dtype combination (%d -> %d)", dtype, out_dtype);
 }
@@ -360,7 +437,7 @@ lce_dlogits_kernel(T* logits, int64_t ld, const int64_t* __restrict__ labels, in
 
 struct LceLayout {
   size_t status = 0, scale = 64;
-  size_t logits, stats, xt, lse, row_ce, row_z, acc, total;
+  size_t logits, stats, xt, lse, row_ce, row_z, acc, dh2, total;
   int64_t chunk, ldl;
   int num_n;
   bool need_acc;
@@ -388,6 +465,9 @@ LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, 
   L.need_acc = !loss_only && fp32_accum && nchunks > 1;
   L.acc = off;
   if (L.need_acc) off = al256(off + sizeof(float) * (size_t)D * V);
+  // second split-K partial of a chunk's dH [chunk, D]
+  L.dh2 = off;
+  if (!loss_only) off = al256(off + (size_t)chunk * D * elt);
   L.total = off;
   return L;
 }
@@ -506,7 +586,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       Operand A{logits, L.ldl, 0};
       Operand B{W, D, 1};
       if ((rc = run_gemm(dtype, A, B, rows, D, V, static_cast<T*>(grad_input) + s0 * D, dtype, D, nullptr, nullptr,
-                         0, nullptr, 1, sms, st, status, PROF_GEMM_DH)))
+                         0, nullptr, 1, sms, st, status, PROF_GEMM_DH, Hints{}, ws + L.dh2)))
         return rc;
     }
   }

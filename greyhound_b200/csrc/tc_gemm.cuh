@@ -59,6 +59,10 @@ struct Params {
   // EPI_STORE
   void* out;
   int64_t ldo;
+  // split-K (EPI_STORE): ksplit slices of K per output tile (0 or 1: none);
+  // slice 0 writes `out`, slice 1 writes `out2` (same pitch), the host sums
+  int ksplit;
+  void* out2;
   int vec_ok;           // 16-byte aligned rows (vector stores allowed)
   const float* add_f32; // optional fp32 addend [M, ldadd]
   const void* add_same; // optional addend in the output type [M, ldadd]
@@ -105,6 +109,23 @@ __device__ __forceinline__ void tile_coords(const Params& p, int tile, int& mt, 
     nt = g * p.group + r % gn;
     mt = r / gn;
   }
+}
+
+// One work unit: output tile (mt, nt) and its K slice [kb0, kb1) of 64-wide
+// k-steps. Split-K units of slice ks follow all units of slice ks - 1.
+struct TileK {
+  int mt, nt, ks, kb0, kb1;
+};
+__device__ __forceinline__ TileK tile_k(const Params& p, int tile, int nkb) {
+  TileK t;
+  const int nsplit = p.ksplit > 1 ? p.ksplit : 1;
+  const int per_slice = p.num_m * p.num_n;
+  t.ks = nsplit > 1 ? tile / per_slice : 0;
+  tile_coords(p, tile - t.ks * per_slice, t.mt, t.nt);
+  const int per = (nkb + nsplit - 1) / nsplit;
+  t.kb0 = t.ks * per;
+  t.kb1 = t.kb0 + per < nkb ? t.kb0 + per : nkb;
+  return t;
 }
 
 template <typename T> struct AbType;
@@ -413,11 +434,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = p.debug_no_loads ? p.num_tiles : unit; tile < p.num_tiles; tile += nunits) {
-        int mt, nt;
-        tile_coords(p, tile, mt, nt);
-        const int ma = mt * G::TM + (int)rank * BM;         // this CTA's A rows
-        const int nb = nt * G::TN + (int)rank * G::HB;      // this CTA's B rows (first half)
-        for (int kb = 0; kb < nkb; ++kb) {
+        const TileK tk = tile_k(p, tile, nkb);
+        const int ma = tk.mt * G::TM + (int)rank * BM;      // this CTA's A rows
+        const int nb = tk.nt * G::TN + (int)rank * G::HB;   // this CTA's B rows (first half)
+        for (int kb = tk.kb0; kb < tk.kb1; ++kb) {
           if (!tc::mbar_wait(&empty[stage], phase ^ 1, abort_flag, lim)) goto producer_done;
           uint8_t* a = sA + stage * G::A_BYTES;
           uint8_t* b = sB + stage * G::B_BYTES;
@@ -495,12 +515,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
         };
         // k-steps [0, pre) open a tile on half 0 while the epilogue still
-        // drains half 1 of the previous tile; k-steps [nkb - tail, nkb) close
+        // drains half 1 of the previous tile; k-steps [nkt - tail, nkt) close
         // it half 0 first, so the epilogue starts on half 0 while the tensor
         // pipe finishes half 1.
-        const int pre = nkb < STG ? nkb : STG;
-        const int tail = nkb - pre < STG ? nkb - pre : STG;
         for (int tile = unit; tile < p.num_tiles; tile += nunits) {
+          const TileK tk = tile_k(p, tile, nkb);
+          const int nkt = tk.kb1 - tk.kb0;  // k-steps of this unit
+          const int pre = nkt < STG ? nkt : STG;
+          const int tail = nkt - pre < STG ? nkt - pre : STG;
           if (!tc::mbar_wait(&tempty[0], acc_phase ^ 1, abort_flag, lim)) break;
           tc::tc_fence_after();
           bool ok = true;
@@ -520,7 +542,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc::mma_commit_pair_mc(&empty[stage], 0x3);
             if (++stage == STG) { stage = 0; phase ^= 1; }
           }
-          for (int kb = pre; kb < nkb - tail; ++kb) {
+          for (int kb = pre; kb < nkt - tail; ++kb) {
             if (!tc::mbar_wait(&full[stage], phase, abort_flag, lim)) { ok = false; break; }
             tc::tc_fence_after();
             issue(stage, 0, false);
@@ -549,11 +571,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       } else
       for (int tile = unit; tile < p.num_tiles; tile += nunits) {
+        const TileK tk = tile_k(p, tile, nkb);
+        const int nkt = tk.kb1 - tk.kb0;
         if (!tc::mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, lim)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = 0; kb < nkt; ++kb) {
           if (!tc::mbar_wait(&full[stage], phase, abort_flag, lim)) { ok = false; break; }
           tc::tc_fence_after();
           const uint32_t a0 = tc::smem_u32(sA + stage * G::A_BYTES);
@@ -591,8 +615,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint32_t xphase = 0;  // bit b: phase of xready[b]
     bool stop = false;
     for (int tile = unit; tile < p.num_tiles && !stop; tile += nunits) {
-      int mt, nt;
-      tile_coords(p, tile, mt, nt);
+      const TileK tk = tile_k(p, tile, nkb);
+      const int mt = tk.mt, nt = tk.nt;
+      void* const pout = tk.ks ? p.out2 : p.out;  // this K slice's output
       const int m0 = mt * G::TM + (int)rank * BM;
       if (NSUB == 1) {
         if (!tc::mbar_wait(&tfull[acc], acc_phase, abort_flag, lim)) break;
@@ -640,7 +665,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const float scale = (EPI == EPI_STORE && p.scale) ? *p.scale : 1.f;
           const int64_t lab = (EPI == EPI_LCE && row_ok) ? p.labels[row] - p.label_offset : -1;
           float* xt_row = EPI == EPI_LCE ? p.xt + row : nullptr;
-          OutT* out = reinterpret_cast<OutT*>(p.out);
+          OutT* out = reinterpret_cast<OutT*>(pout);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             if (!tc::mbar_wait(&tfull[h], acc_phase, abort_flag, lim)) { stop = true; break; }
@@ -729,8 +754,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                   w[sc * 8 + j] = pack2<OutT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
               }
               lce_fold_chunk<OutT>(w, c, n0, p.N, lab_rel, p.xt + row, m_run, s_run);
-              if (p.out)
-                store_chunk_packed<OutT>(reinterpret_cast<OutT*>(p.out), p.ldo, m0 + q * 32, p.M, n0 + c * 32, p.N, w,
+              if (pout)
+                store_chunk_packed<OutT>(reinterpret_cast<OutT*>(pout), p.ldo, m0 + q * 32, p.M, n0 + c * 32, p.N, w,
                                          stage_out, lane, p.vec_ok, p.out_evict_first);
             }
             // group 1 hands its (max, sum) to group 0, which writes the half's stats
@@ -762,7 +787,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                   for (int j = 0; j < 32; ++j) v[j] += a[j];
                 }
-                store_chunk<OutT>(reinterpret_cast<OutT*>(p.out), p.ldo, m0 + q * 32, p.M, col0, p.N, v, stage_out,
+                store_chunk<OutT>(reinterpret_cast<OutT*>(pout), p.ldo, m0 + q * 32, p.M, col0, p.N, v, stage_out,
                                   lane, p.vec_ok, p.out_evict_first);
               }
             }
