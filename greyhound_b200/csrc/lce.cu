@@ -723,10 +723,12 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
   const int elt = elt_size(dtype);
   Operand A{ws + L.logits + (size_t)row_begin * L.ldl * elt, L.ldl, 0};
   Operand B{W, D, 1};
+  // each row range has its own rows of the split-K partial buffer, so the two
+  // ranges may run concurrently
   return run_gemm(dtype, A, B, row_end - row_begin, D, V,
                   static_cast<char*>(grad_input) + (s0 + row_begin) * D * elt, dtype, D, nullptr, nullptr, 0,
                   nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status),
-                  PROF_GEMM_DH);
+                  PROF_GEMM_DH, Hints{}, ws + L.dh2 + (size_t)row_begin * D * elt);
 }
 
 extern "C" int gh_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
