@@ -465,7 +465,7 @@ def bench_reference(args, rank, world):
     """CPU restatement of the reference (the oracle) on the host cores."""
     if rank != 0:
         return None
-    N, D, V = 8192, 4096, 128256
+    N, D, V = args.rows or 8192, args.hidden or 4096, args.vocab or 128256
     per_step = []
     for _ in range(args.warmup + args.steps):
         b = cpu_baseline_lce(N, D, V, budget_s=args.ref_step_seconds)

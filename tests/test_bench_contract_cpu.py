@@ -1,0 +1,29 @@
+"""The reference arm of bench.py (the oracle port on host cores) prints one
+JSON line with the keys the driver reads; checked here at a tiny shape."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_reference_arm_prints_the_contract_line():
+    res = subprocess.run(
+        [sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "3",
+         "--ref-step-seconds", "0.2", "--rows", "64", "--hidden", "128", "--vocab", "1000"],
+        cwd=ROOT, capture_output=True, text=True, timeout=300,
+    )
+    assert res.returncode == 0, res.stderr[-2000:]
+    lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["value"] > 0
+    assert d["steps"] == 2 and d["warmup"] >= 3
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["value"] == d["value"] and d["e2e"]["h2d_bytes_per_step"] == 0
+    assert d["config"]["D"] == 128 and d["config"]["V"] == 1000
