@@ -14,9 +14,11 @@ weak scaling, ``value`` = total tokens/s over all ranks.
 One JSON line is printed by rank 0. Timing: W warm-up steps, then K steps
 between barrier + synchronize, device time from CUDA events, max over ranks.
 ``--workload ce`` / ``sls`` time the standalone row kernels (GB/s).
-``--impl reference`` times the CPU restatement of the reference algorithm
-(the oracle; the reference itself is Python/CuTe-DSL and GPU-only for the
-gradient path) on the host cores.
+``--impl reference`` times the reference's own PyTorch path on the host cores
+(bf16 ``F.linear``, ``F.cross_entropy`` on fp32 logits, autograd backward:
+oracle/torch_path.py) on contiguous row samples of the same workload; the
+reference's fused kernels are CuTe-DSL and GPU-only, and its checkout is not
+on the GPU box.
 """
 
 from __future__ import annotations
@@ -190,41 +192,16 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
-_CPU_W: dict = {}
+def cpu_baseline_lce(N, D, V, rows=512, repeats=3):
+    """The reference's own torch path (bf16 F.linear, F.cross_entropy on fp32
+    logits, autograd backward) on one contiguous row sample of the workload,
+    on all host threads (oracle/torch_path.py)."""
+    from oracle.torch_path import time_linear_ce
 
-
-def cpu_baseline_lce(N, D, V, budget_s=12.0, rows_per_sample=64):
-    """Oracle (numpy, fp32 BLAS on all host threads) on row samples of the workload."""
-    import numpy as np
-
-    from oracle import gh_oracle as O
-
-    rng = np.random.default_rng(2)
-    key = (V, D)
-    if key not in _CPU_W:  # the weight and its fp32 gradient accumulator, built once per process
-        gen = torch.Generator().manual_seed(2)
-        W = (torch.randn(V, D, generator=gen) * 0.02).to(torch.bfloat16).float().numpy()
-        _CPU_W.clear()
-        _CPU_W[key] = (W, np.zeros((D, V), dtype=np.float32))
-    W, acc = _CPU_W[key]
-    done = 0
-    t0 = time.perf_counter()
-    while True:
-        H = rng.standard_normal((rows_per_sample, D), dtype=np.float32)
-        H = O.round_bf16(H / np.sqrt((H * H).mean(1, keepdims=True) + 1e-6))
-        t = rng.integers(0, V, size=rows_per_sample)
-        O.chunk_step(H, W, t, 0.0, -100, "bf16", acc)
-        done += rows_per_sample
-        if time.perf_counter() - t0 >= budget_s:
-            break
-    el = time.perf_counter() - t0
-    return {
-        "value": done / el,
-        "unit": "tokens/s",
-        "cores": cpu_threads(),
-        "kind": "port",
-        "sample": f"{done} rows of the {N}x{D}x{V} workload in {rows_per_sample}-row chunks of the reference loop (logits, CE+grad, dH, fp32 dW accumulate), {el:.1f}s",
-    }
+    r = time_linear_ce(N, D, V, rows=rows, repeats=repeats, threads=os.cpu_count() or 1)
+    r["kind"] = "port"
+    r["port_of"] = "reference torch path (src/tests/nn/functional/chunked_linear_loss_test.py:18-42)"
+    return r
 
 
 def bench_lce(args, rank, world, local):
@@ -233,6 +210,9 @@ def bench_lce(args, rank, world, local):
 
     N, D, V = args.rows or 8192, args.hidden or 4096, args.vocab or 128256
     dev = torch.device("cuda", local)
+    # the standalone row kernels at their configs (cfg2, cfg4), measured first,
+    # on a GPU not yet heated by the GEMMs
+    rows_block = row_kernel_block(local) if world == 1 and not args.no_extras else None
     H, W, t = make_lce_inputs(N, D, V, 2 + rank, dev)
     H.requires_grad_(True)
     W.requires_grad_(True)
@@ -261,6 +241,13 @@ def bench_lce(args, rank, world, local):
     prof = _lib.profile_read(reset=True)
     launches = (_lib.launch_count() - c0) // (args.steps + args.warmup)
     clocks = clk.summary()
+    # peak device memory of one step, measured as the reference bench does
+    # (src/benchmarks/chunked_linear_cross_entropy_bench.py:182-190)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats(dev)
+    step()
+    torch.cuda.synchronize()
+    peak_mem_mb = torch.cuda.max_memory_allocated(dev) / 2**20
 
     # end-to-end: each step's H/targets copied from pinned host memory and its
     # loss read back. The copy of step k+1's inputs is issued on a copy stream
@@ -328,17 +315,12 @@ def bench_lce(args, rank, world, local):
             kernels[cls] = k
     gemms = [c for c in kernels if c.startswith("gemm_") and c != "gemm_other"]
     dom = max(gemms, key=lambda c: kernels[c]["share_of_step"], default=None)
-    peak_sus = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    timed_s = ms * args.steps * 1e-3
     if dom is not None:
         ach = kernels[dom]["tflops"]
-        roofline = {
-            "bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak_sus, "unit": "TFLOP/s",
-            "frac": ach / peak_sus,
-            "peak_source": f"{peak_src} sustained cuBLAS bf16 (kernel timed inside a long step)",
-            "frac_of_burst_peak": ach / peaks["bf16_tflops"], "frac_of_spec_2250": ach / 2250.0,
-            "algorithmic_flops_per_launch": gemm_flops,
-            "traffic": TRAFFIC_BYTES_PER_LAUNCH.get(dom),
-        }
+        roofline = roofline_tensor(ach, peaks, peak_src, timed_s)
+        roofline.update(kernel=dom, algorithmic_flops_per_launch=gemm_flops,
+                        traffic=TRAFFIC_BYTES_PER_LAUNCH.get(dom))
     else:
         roofline = None
     line = {
@@ -377,12 +359,138 @@ def bench_lce(args, rank, world, local):
         "gpu_launches": launches * args.steps,
         "gpu_launches_per_step": launches,
         "clocks": clocks,
+        "peak_mem_mb": peak_mem_mb,
     }
+    del H, W, bufs
+    torch.cuda.empty_cache()
+    if rows_block is not None:
+        line["row_kernels"] = rows_block
+    if world == 1 and not args.no_extras and (N, D, V) == (8192, 4096, 128256):
+        # same-box comparators, so the driver's run measures them too
+        line["comparators"] = comparators(args)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        del H, W, bufs
-        torch.cuda.empty_cache()
         line["cpu_baseline"] = cpu_baseline_lce(N, D, V)
     return line
+
+
+def roofline_tensor(ach: float, peaks: dict, src: str, timed_s: float) -> dict:
+    """Tensor-core roofline of a kernel timed over ``timed_s`` seconds: the
+    burst cuBLAS peak for a short timed region (the clocks stay near maximum),
+    the sustained one (measured over 4 s at the 1 kW cap) for >= 4 s."""
+    sustained = timed_s >= 4.0 and "bf16_tflops_sustained" in peaks
+    peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    r = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+         "peak_source": f"{src} {'sustained' if sustained else 'burst'} cuBLAS bf16 "
+                        f"(timed region {timed_s:.2f} s)",
+         "frac_of_spec_2250": ach / 2250.0}
+    if "bf16_tflops_sustained" in peaks:
+        r["frac_of_sustained_peak"] = ach / peaks["bf16_tflops_sustained"]
+    return r
+
+
+def _row_case(which: str, rows: int, V: int, dev, steps: int = 30, warmup: int = 10) -> dict:
+    from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad
+    from greyhound_b200.kernels.logprobs import (
+        selective_log_softmax_backward_kernel,
+        selective_log_softmax_with_lse,
+    )
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1 if which == "ce" else 3)
+    if which == "ce":
+        x = (torch.randn(rows, V, device=dev, generator=g) * 2).to(torch.bfloat16)
+        t = torch.randint(0, V, (rows,), device=dev, generator=g)
+        out = torch.empty_like(x)
+        step = lambda: cross_entropy_with_grad(x, t, 0.0, -100, out, mean_reduction=True)  # noqa: E731
+        nbytes = 2 * rows * V * 2 + rows * 8
+    else:
+        x = (torch.randn(rows, V, device=dev, generator=g) * 3).to(torch.bfloat16)
+        t = torch.randint(0, V, (rows,), device=dev, generator=g)
+        if which == "sls":
+            step = lambda: selective_log_softmax_with_lse(x, t, out_dtype=torch.float32)  # noqa: E731
+            nbytes = rows * V * 2 + rows * 8 + rows * 4
+        else:
+            _, lse = selective_log_softmax_with_lse(x, t, out_dtype=torch.float32)
+            go = torch.randn(rows, device=dev, generator=g)
+            step = lambda: selective_log_softmax_backward_kernel(x, t, lse, go)  # noqa: E731
+            nbytes = 2 * rows * V * 2 + rows * (8 + 4 + 4)
+    ms = time_steps(step, steps, warmup, 1)
+    del x
+    torch.cuda.empty_cache()
+    return {"rows": rows, "V": V, "ms": ms, "gbs": nbytes / (ms * 1e-3) / 1e9, "algorithmic_bytes": nbytes}
+
+
+def row_kernel_block(local: int) -> dict:
+    """CE fwd+grad on [4096, 128256] and [16, 128256] (cfg2), selective
+    log-softmax forward and backward on [65536, 151936] (cfg4), bf16; GB/s of
+    algorithmic bytes and the fraction of the measured HBM copy bandwidth.
+    The big cases' inputs exceed L2; the 16-row case is L2-resident and
+    latency-bound, reported for completeness."""
+    dev = torch.device("cuda", local)
+    peaks, src = load_peaks()
+    out = {"peak_gbs": peaks["hbm_gbs"], "peak_source": f"{src} HBM copy"}
+    for name, which, rows, V in (("ce_cfg2", "ce", 4096, 128256), ("ce_cfg2_16rows", "ce", 16, 128256),
+                                 ("sls_fwd_cfg4", "sls", 65536, 151936), ("sls_bwd_cfg4", "sls_bwd", 65536, 151936)):
+        r = _row_case(which, rows, V, dev)
+        r["frac"] = r["gbs"] / peaks["hbm_gbs"]
+        out[name] = r
+    return out
+
+
+def comparators(args) -> dict:
+    """Same-box comparators of the cfg3 step, each in a child process with a
+    time limit: the reference's own GPU implementation
+    (``greyhound.nn.functional.chunked_linear_cross_entropy``, installed
+    unmodified under baseline/_ref), and the reference bench's torch-eager
+    and torch-compile providers (src/benchmarks/third_party/torch.py)."""
+    res = {}
+    for prov in ("greyhound_reference", "torch_eager", "torch_compile"):
+        cmd = [sys.executable, str(ROOT / "bench.py"), "--comparator-child", prov,
+               "--steps", "10", "--warmup", "3"]
+        try:
+            p = subprocess.run(cmd, capture_output=True, text=True, timeout=420)
+            last = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+            res[prov] = json.loads(last[-1]) if last else {
+                "unavailable": (p.stderr.strip().splitlines() or ["no output"])[-1][:300]}
+        except subprocess.TimeoutExpired:
+            res[prov] = {"unavailable": "timed out after 420 s"}
+    return res
+
+
+def comparator_child(prov: str, steps: int, warmup: int) -> dict:
+    N, D, V = 8192, 4096, 128256
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    H, W, t = make_lce_inputs(N, D, V, 2, dev)
+    H.requires_grad_(True)
+    W.requires_grad_(True)
+    if prov == "greyhound_reference":
+        ref = ROOT / "baseline" / "_ref"
+        if not (ref / "greyhound").exists():
+            return {"unavailable": "reference not installed under baseline/_ref"}
+        sys.path.insert(0, str(ref))
+        from greyhound.nn.functional import chunked_linear_cross_entropy as fn
+    else:
+        import torch.nn.functional as F
+
+        def fn(inputs, weight, target):  # src/benchmarks/third_party/torch.py:9-30
+            logits = inputs @ weight.T
+            return F.cross_entropy(logits.float(), target, ignore_index=-100, reduction="mean")
+
+        if prov == "torch_compile":
+            fn = torch.compile(fn)
+
+    def step():
+        H.grad = None
+        W.grad = None
+        fn(H, W, t).backward()
+
+    ms = time_steps(step, steps, warmup, 1)
+    torch.cuda.reset_peak_memory_stats(dev)
+    step()
+    torch.cuda.synchronize()
+    return {"ms_per_step": ms, "tokens_per_s": N / (ms * 1e-3), "tflops": 6.0 * N * D * V / (ms * 1e-3) / 1e12,
+            "peak_mem_mb": torch.cuda.max_memory_allocated(dev) / 2**20, "steps": steps, "warmup": warmup}
 
 
 def bench_lce70b(args, rank, world, local):
@@ -453,27 +561,28 @@ def bench_lce70b(args, rank, world, local):
         "config": {"workload": "Llama-3-70B-scale head chunked_linear_cross_entropy fwd+bwd (BASELINE configs[4])",
                    "N": N, "D": D, "V": V, "parallelism": par, "l2": "inputs larger than L2"},
         "tflops_per_gpu": tflops_gpu,
-        "roofline": {"bound": "tensor", "kernel": "whole step (6*N*D*V / GPUs)", "achieved": tflops_gpu,
-                     "peak": peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]), "unit": "TFLOP/s",
-                     "frac": tflops_gpu / peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]),
-                     "peak_source": src, "traffic": None},
+        "roofline": dict(roofline_tensor(tflops_gpu, peaks, src, ms * args.steps * 1e-3),
+                         kernel="whole step (6*N*D*V / GPUs)", traffic=None),
         "kernels": kernels, "gpu_launches": launches * args.steps, "clocks": clk.summary(),
     }
 
 
 def bench_reference(args, rank, world):
-    """CPU restatement of the reference (the oracle) on the host cores."""
+    """The reference's own torch path (oracle/torch_path.py) on the host cores:
+    each step is one contiguous ``--ref-rows``-row sample of the workload
+    (forward, backward, one dW), tokens/s = sample rows / sample time. Rank 0
+    alone runs it."""
     if rank != 0:
         return None
+    from oracle.torch_path import time_linear_ce
+
     N, D, V = args.rows or 8192, args.hidden or 4096, args.vocab or 128256
-    per_step = []
-    for _ in range(args.warmup + args.steps):
-        b = cpu_baseline_lce(N, D, V, budget_s=args.ref_step_seconds)
-        per_step.append(b)
-    vals = [b["value"] for b in per_step[args.warmup:]]
-    v = statistics.median(vals) if vals else per_step[-1]["value"]
-    cb = dict(per_step[-1])
-    cb["value"] = v
+    rows = min(args.ref_rows, N)
+    r = time_linear_ce(N, D, V, rows=rows, repeats=args.warmup + args.steps, threads=os.cpu_count() or 1)
+    v = r["value"]
+    cb = {"value": v, "unit": "tokens/s", "cores": r["cores"], "kind": "port",
+          "port_of": "reference torch path (src/tests/nn/functional/chunked_linear_loss_test.py:18-42)",
+          "sample": r["sample"]}
     return {
         "impl": "reference",
         "metric": METRIC,
@@ -486,10 +595,13 @@ def bench_reference(args, rank, world):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f32 (numpy BLAS on bf16-rounded values)",
+        "dtype": "bf16 GEMMs, fp32 CE (torch CPU)",
         "data": "synthetic",
-        "config": {"workload": "Llama-3-8B LM head chunked_linear_cross_entropy fwd+bwd (BASELINE configs[2])",
-                   "N_per_rank": N, "D": D, "V": V, "parallelism": "host CPU"},
+        "config": {"workload": "Llama-3-8B LM head chunked_linear_cross_entropy fwd+bwd (BASELINE configs[2])"
+                   if (N, D, V) == (8192, 4096, 128256) else f"profiling case N={N} D={D} V={V}",
+                   "N_per_rank": N, "D": D, "V": V, "global_tokens": N * world,
+                   "reduction": "mean", "ignore_frac": 0.02, "parallelism": "host CPU",
+                   "l2": "n/a (host)"},
         "cpu_baseline": cb,
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -557,7 +669,9 @@ def main() -> int:
     ap.add_argument("--workload", choices=["lce", "lce70b", "ce", "sls", "sls_bwd"], default="lce")
     ap.add_argument("--parallel", choices=["rows", "vocab"], default="rows", help="lce70b sharding mode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ref-step-seconds", type=float, default=5.0)
+    ap.add_argument("--no-extras", action="store_true", help="skip the row-kernel block and the comparators")
+    ap.add_argument("--comparator-child", default="", help=argparse.SUPPRESS)
+    ap.add_argument("--ref-rows", type=int, default=512, help="rows per sample of the reference CPU arm")
     # shape overrides, only for small profiler captures (the default is the workload)
     ap.add_argument("--rows", type=int, default=0)
     ap.add_argument("--hidden", type=int, default=0)
@@ -565,6 +679,9 @@ def main() -> int:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.comparator_child:
+        print(json.dumps(comparator_child(args.comparator_child, args.steps, args.warmup)), flush=True)
+        return 0
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))

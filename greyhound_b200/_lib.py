@@ -81,10 +81,18 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
+    "gh_lce_dw_peers": (_i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, ctypes.POINTER(_vp), _i32, _i64, _vp, _sz, _vp]),
+    "gh_sum_slots": (_i32, [_vp, _i32, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),
+    "gh_ipc_get_handle": (_i32, [_vp, _vp, ctypes.POINTER(_sz)]),
+    "gh_ipc_open": (_i32, [_vp, _sz, ctypes.POINTER(_vp)]),
+    "gh_ipc_close": (_i32, [_vp, _sz]),
+    "gh_take_device_errors": (_i32, [_i32]),
+    "gh_ce_noalloc_status": (_i32, [ctypes.POINTER(ctypes.c_int), _vp]),
     "gh_profile_enable": (None, [_i32]),
     "gh_profile_read": (_i32, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong), _i32, _i32]),
 }
 GH_LCE_DEFER_LAST_DH = 1
+GH_LCE_KEEP_DW_OPERAND = 2
 PROF_CLASSES = ("gemm_logits_ce", "gemm_dw", "gemm_dh", "dlogits", "rows", "gemm_other")
 
 _lock = threading.Lock()
@@ -182,6 +190,7 @@ def scaled(t: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
         return t * g
     if not (t.is_contiguous() or t.T.is_contiguous()) or t.data_ptr() % 16:
         return t * g
+    raise_pending(t.device, "backward")
     out = torch.empty_like(t)  # preserves the (possibly transposed) dense layout
     gf = g.detach().reshape(1).to(torch.float32)
     check(load().gh_scale(t.data_ptr(), out.data_ptr(), t.numel(), dtype_code(t.dtype), gf.data_ptr(),
@@ -192,15 +201,49 @@ def scaled(t: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
 CHECK_STATUS = os.environ.get("GREYHOUND_B200_CHECK", "0") not in ("", "0")
 
 
+def take_device_errors(device: torch.device | int | None = None) -> int:
+    """Read and clear the sticky device-error bits of a device (no sync).
+
+    Every library call ends by OR-ing its workspace status word into a
+    per-device slot of pinned host memory on the GPU; this returns the bits
+    that calls which have already run on the GPU left there."""
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, int):
+        idx = device
+    else:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+    return int(load().gh_take_device_errors(idx))
+
+
+def _raise_bits(bits: int, what: str) -> None:
+    if bits & GH_DEV_BAD_LABEL:
+        raise ValueError(f"{what}: a target / index outside [0, vocab) that is not ignore_index "
+                         "(recorded on the device by an earlier greyhound_b200 call)")
+    if bits:
+        raise GreyhoundLibraryError(f"{what}: device status {bits:#x} (a GEMM pipeline wait timed out "
+                                    "in an earlier greyhound_b200 call; its results are not valid)")
+
+
+def raise_pending(device: torch.device, what: str) -> None:
+    """Raise for problems that earlier calls on ``device`` recorded on the GPU:
+    ValueError for a label outside [0, V), RuntimeError for a pipeline timeout.
+    Called on entry to every op and in the autograd backward; it does not
+    synchronise, so a problem surfaces at the first call after the GPU has
+    run the call that recorded it."""
+    bits = take_device_errors(device)
+    if bits:
+        _raise_bits(bits, what)
+
+
 def raise_on_status(ws: torch.Tensor, what: str) -> None:
-    """With GREYHOUND_B200_CHECK=1: synchronise and raise if the kernels of the
-    last call recorded a problem in the workspace status word (a label outside
-    [0, V): ValueError; a pipeline timeout: RuntimeError). Off by default: the
-    status word is written on the device and reading it costs a host sync."""
+    """With GREYHOUND_B200_CHECK=1: synchronise and raise at once if the
+    kernels of the last call recorded a problem in the workspace status word
+    (a label outside [0, V): ValueError; a pipeline timeout: RuntimeError).
+    Without it the same bits surface through ``raise_pending`` on the next
+    call, without a host sync."""
     if not CHECK_STATUS:
         return
     st = device_status(ws)
-    if st & GH_DEV_BAD_LABEL:
-        raise ValueError(f"{what}: a target / index outside [0, vocab) that is not ignore_index")
-    if st:
-        raise GreyhoundLibraryError(f"{what}: device status {st:#x} (pipeline timeout)")
+    take_device_errors(ws.device)  # reported here; do not report it twice
+    _raise_bits(st, what)

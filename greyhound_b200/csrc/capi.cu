@@ -2,6 +2,8 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -26,7 +28,63 @@ int check_launch(const char* what) {
 
 void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+// ---------------------------------------------------------------------------
+// Sticky device-error bits, one int per device index, in pinned host memory
+// that the GPU writes directly. Every entry point that owns a workspace status
+// word ends with publish_status(): a one-thread kernel that ORs a non-zero
+// status into this device's slot (nothing crosses the bus when the status is
+// zero). The host reads and clears a slot with gh_take_device_errors() without
+// synchronising, so a problem recorded by call k is seen at call k + 1 or
+// later, once the GPU has run call k.
+namespace {
+constexpr int kMaxDevices = 64;
+std::once_flag g_slots_once;
+int* g_slots = nullptr;
+
+__global__ void publish_status_kernel(const int* __restrict__ status, int* slot) {
+  const int v = *reinterpret_cast<const volatile int*>(status);
+  if (v) {
+    volatile int* h = slot;
+    *h = *h | v;
+  }
+}
+}  // namespace
+
+int* error_slots() {
+  std::call_once(g_slots_once, [] {
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, kMaxDevices * sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess) {
+      memset(p, 0, kMaxDevices * sizeof(int));
+      g_slots = static_cast<int*>(p);
+    } else {
+      cudaGetLastError();
+    }
+  });
+  return g_slots;
+}
+
+int publish_status(const int* status, cudaStream_t st) {
+  if (!status) return GH_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(GH_EUNSUPPORTED, "device index %d out of range", dev);
+  int* slots = error_slots();
+  if (!slots) return set_error(GH_ECUDA, "could not allocate the pinned device-error slots");
+  void* dslot = nullptr;
+  e = cudaHostGetDevicePointer(&dslot, slots + dev, 0);
+  if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaHostGetDevicePointer: %s", cudaGetErrorString(e));
+  publish_status_kernel<<<1, 1, 0, st>>>(status, static_cast<int*>(dslot));
+  count_launch(1);
+  return check_launch("publish_status");
+}
+
 }  // namespace gh
+
+extern "C" int gh_take_device_errors(int device) {
+  if (device < 0 || device >= gh::kMaxDevices || !gh::g_slots) return 0;
+  return __atomic_exchange_n(&gh::g_slots[device], 0, __ATOMIC_SEQ_CST);
+}
 
 extern "C" int gh_abi_version(void) { return 1; }
 extern "C" const char* gh_last_error_string(void) { return gh::g_err; }

@@ -24,6 +24,9 @@ constexpr float kNegInf = -__builtin_huge_valf();
 int set_error(int code, const char* fmt, ...);
 int check_launch(const char* what);
 void count_launch(int n = 1);
+// Enqueue the copy of a non-zero workspace status word into this device's
+// sticky error slot (gh_take_device_errors); GH_OK when status is NULL.
+int publish_status(const int* status, cudaStream_t st);
 
 // Kernel classes for the optional event timing (gh_profile_enable / _read).
 enum ProfClass {

@@ -144,7 +144,7 @@ template <typename T, int EPI, typename OutT>
 int launch_gemm_mm(const CUtensorMap& ta, const CUtensorMap& tb, int a_mn, int b_mn, int pair, int nsub,
                    gemm::Params& p, int max_ctas, cudaStream_t st) {
   if (pair == 2 && nsub == 2) {
-    if constexpr (sizeof(OutT) == 2) {
+    if constexpr (sizeof(OutT) == 2 && EPI != gemm::EPI_LCE_Q) {
       if (p.add_f32 || p.add_same) return set_error(GH_EUNSUPPORTED, "512-column GEMM tile with an addend");
       if (!a_mn && !b_mn) return launch_gemm_t<T, 0, 0, EPI, OutT, 2, 2>(ta, tb, p, max_ctas, st);
       if (!a_mn && b_mn) return launch_gemm_t<T, 0, 1, EPI, OutT, 2, 2>(ta, tb, p, max_ctas, st);
@@ -306,10 +306,19 @@ int add_partial(void* out, const void* part, int64_t rows, int64_t cols, int64_t
   return check_launch("add_partial");
 }
 
+// Output rows split into bands stored on the ranks that reduce them
+// (gemm::Params::peer_out).
+struct PeerOut {
+  int n = 0;
+  int64_t rows = 0;
+  void* ptr[gemm::kMaxPeers] = {};
+};
+
 int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N, int64_t K, void* out,
              int out_dtype, int64_t ldo, const float* add_f32, const void* add_same, int64_t ldadd,
              const float* scale, int raster, int max_ctas, cudaStream_t st, int* status,
-             int prof_class = PROF_GEMM_OTHER, Hints hints = Hints{}, void* split_out = nullptr) {
+             int prof_class = PROF_GEMM_OTHER, Hints hints = Hints{}, void* split_out = nullptr,
+             const float* row_scale = nullptr, const PeerOut* peers = nullptr) {
   if (M <= 0 || N <= 0) return GH_OK;
   if (K <= 0) return set_error(GH_EINVAL, "GEMM needs K >= 1");
   ProfScope prof(prof_class, st);
@@ -340,6 +349,18 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
   p.add_same = add_same;
   p.ldadd = ldadd;
   p.scale = scale;
+  p.row_scale = row_scale;
+  if (peers && peers->n > 0) {
+    if (out_dtype == GH_F32 || split_out || peers->n > gemm::kMaxPeers || peers->rows % (2 * BM))
+      return set_error(GH_EUNSUPPORTED, "peer output: 16-bit output, no split-K, <= %d bands of a multiple of %d rows",
+                       gemm::kMaxPeers, 2 * BM);
+    p.npeer = peers->n;
+    p.peer_rows = peers->rows;
+    for (int i = 0; i < peers->n; ++i) {
+      p.peer_out[i] = peers->ptr[i];
+      if (reinterpret_cast<uintptr_t>(peers->ptr[i]) & 15) p.vec_ok = 0;
+    }
+  }
   p.status = status;
   p.a_hint = hints.a;
   p.b_hint = hints.b;
@@ -371,24 +392,48 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
 // (lse_shard, 1, target logit or -inf) for the cross-shard exchange instead of
 // loss terms.
 constexpr int kCombineWarps = 8;
+// q mode (qm != nullptr): the logits GEMM stored q = e^x per 128-column group
+// (or raw logits, flagged in qm); also write alpha[r], the factor that turns
+// the row's stored values into its logits gradient (s (1 + 2 z lse) e^-lse
+// for a q row, s for a row the fix-up pass rewrites, 0 for an ignored row),
+// and rowflag[r] = 1 when the row needs that fix-up.
+struct QOut {
+  const uint8_t* qm;
+  const float* scale;  // s (nullptr: 1)
+  float zmul;
+  float* alpha;
+  int* rowflag;
+};
+
 __global__ void __launch_bounds__(32 * kCombineWarps)
 lce_combine_kernel(const float2* __restrict__ stats, int num_n, int64_t rows, const float* __restrict__ xt,
                    const int64_t* __restrict__ labels, int64_t label_offset, int64_t V, int64_t ignore,
-                   float* lse_out, float* row_ce, float* row_z, float* stats3, int* status) {
+                   float* lse_out, float* row_ce, float* row_z, float* stats3, int* status, QOut qo) {
   __shared__ float sm[kCombineWarps][32], ss[kCombineWarps][32];
+  __shared__ int sf[kCombineWarps][32];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t r = (int64_t)blockIdx.x * 32 + lane;
   MS acc = ms_empty();
+  int flag = 0;
   if (r < rows)
     for (int j = w; j < num_n; j += kCombineWarps) {
       const float2 p = stats[(int64_t)j * rows + r];
       acc = ms_merge(acc, MS{p.x, p.y});
+      if (qo.qm) {
+        // a group is only written when it has columns inside the vocabulary
+        flag |= qo.qm[((int64_t)j * 2) * rows + r];
+        if ((int64_t)j * BN + BN / 2 < V) flag |= qo.qm[((int64_t)j * 2 + 1) * rows + r];
+      }
     }
   sm[w][lane] = acc.m;
   ss[w][lane] = acc.s;
+  sf[w][lane] = flag;
   __syncthreads();
   if (w != 0 || r >= rows) return;
-  for (int k = 1; k < kCombineWarps; ++k) acc = ms_merge(acc, MS{sm[k][lane], ss[k][lane]});
+  for (int k = 1; k < kCombineWarps; ++k) {
+    acc = ms_merge(acc, MS{sm[k][lane], ss[k][lane]});
+    flag |= sf[k][lane];
+  }
   const float lse = (acc.m + fast_log2(acc.s)) * kLn2;
   const int64_t t = labels[r];
   const int64_t loc = t - label_offset;
@@ -407,6 +452,82 @@ lce_combine_kernel(const float2* __restrict__ stats, int num_n, int64_t rows, co
   lse_out[r] = lse;
   row_ce[r] = valid ? lse - xt[r] : 0.f;
   row_z[r] = valid ? lse * lse : 0.f;
+  if (qo.qm) {
+    const float s = qo.scale ? *qo.scale : 1.f;
+    const float f = 1.f + 2.f * qo.zmul * lse;
+    flag |= fabsf(f) < 1e-3f;
+    qo.alpha[r] = !valid ? 0.f : flag ? s : s * f * fast_exp2(-lse * kLog2e);
+    qo.rowflag[r] = valid && flag;
+  }
+}
+
+// Fix-up of the rows that q mode cannot represent: a group whose largest
+// logit lies outside the exponent window (stored raw), or a row whose z-loss
+// factor 1 + 2 z lse is about 0. The row is rewritten as its logits gradient
+// divided by s, (1 + 2 z lse) e^(x - lse) - onehot, from raw logits where a
+// group holds them and from q = e^x elsewhere; its alpha is s. Grid (rows);
+// rows without the flag return at once.
+template <typename T>
+__global__ void __launch_bounds__(256)
+lce_q_fixup_kernel(T* q, int64_t ld, const uint8_t* __restrict__ qm, const int* __restrict__ rowflag,
+                   const float* __restrict__ lse, const int64_t* __restrict__ labels, int64_t label_offset,
+                   int64_t rows, int64_t V, float zmul) {
+  const int64_t row = blockIdx.x;
+  if (!rowflag[row]) return;
+  const float l = lse[row];
+  const float l2 = l * kLog2e;
+  const float f = 1.f + 2.f * zmul * l;
+  const int64_t t = labels[row] - label_offset;
+  T* y = q + row * ld;
+  for (int64_t c = threadIdx.x; c < V; c += blockDim.x) {
+    const int64_t grp = (c >> 8) * 2 + ((c >> 7) & 1);
+    const float v = Elt<T>::to_f(y[c]);
+    float p;
+    if (qm[grp * rows + row]) p = fast_exp2(fmaf(v, kLog2e, -l2));
+    else p = v > 0.f ? fast_exp2(fast_log2(v) - l2) : 0.f;
+    y[c] = Elt<T>::from_f(f * p - (c == t ? 1.f : 0.f));
+  }
+}
+
+// out[r, :] = alpha[r] * H[r, :]: the dW GEMM's second operand in q mode.
+template <typename T>
+__global__ void __launch_bounds__(256)
+scale_rows_kernel(const T* __restrict__ H, const float* __restrict__ alpha, int64_t rows, int64_t D,
+                  T* __restrict__ out) {
+  constexpr int PER = 16 / sizeof(T);
+  const int64_t vpr = D / PER;
+  const int64_t n = rows * vpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / vpr;
+    const float a = alpha[r];
+    Vec16<T> v;
+    v.raw = ld16(reinterpret_cast<const uint4*>(H) + i);
+    float f[PER];
+    v.to_float(f);
+#pragma unroll
+    for (int k = 0; k < PER; ++k) f[k] *= a;
+    v.from_float(f);
+    st16(reinterpret_cast<uint4*>(out) + i, v.raw);
+  }
+}
+
+// Target column of the q-mode rows that the fix-up pass does not rewrite:
+// q[r, t] = e^x_t - e^lse / (1 + 2 z lse), so that alpha[r] * q[r, t] =
+// s (1 + 2 z lse) p_t - s, the reference's logits gradient at the target.
+// Computed from the fp32 target logit (not from the rounded q), so the
+// difference keeps its precision when p_t is close to 1 and is rounded once.
+template <typename T>
+__global__ void __launch_bounds__(256)
+lce_q_target_kernel(T* q, int64_t ld, const int64_t* __restrict__ labels, const float* __restrict__ xt,
+                    const float* __restrict__ lse, const int* __restrict__ rowflag, const float* __restrict__ alpha,
+                    int64_t rows, int64_t V, int64_t ignore, float zmul) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const int64_t t = labels[r];
+  if (t == ignore || t < 0 || t >= V || rowflag[r] || alpha[r] == 0.f) return;
+  const float l = lse[r];
+  const float v = fast_exp2(xt[r] * kLog2e) - fast_exp2(l * kLog2e) / (1.f + 2.f * zmul * l);
+  q[r * ld + t] = Elt<T>::from_f(v);
 }
 
 // In-place logits -> dlogits over a pitched [rows, ld] buffer; grid (rows, chunks).
@@ -438,10 +559,22 @@ lce_dlogits_kernel(T* logits, int64_t ld, const int64_t* __restrict__ labels, in
 struct LceLayout {
   size_t status = 0, scale = 64;
   size_t logits, stats, xt, lse, row_ce, row_z, acc, dh2, total;
+  // q mode only
+  size_t qmode = 0, alpha = 0, rowflag = 0, hs = 0;
   int64_t chunk, ldl;
   int num_n;
   bool need_acc;
+  bool q = false;
 };
+
+// q mode: the logits GEMM stores q = e^x (bf16) instead of the logits, and
+// the gradient GEMMs apply the per-row factor and the one-hot term, so no
+// pass reads and rewrites the [chunk, V] buffer. bf16 only (fp16's exponent
+// range cannot hold e^x); GREYHOUND_B200_LCE_Q=0 switches it off.
+inline bool q_mode_for(int dtype) {
+  const char* e = getenv("GREYHOUND_B200_LCE_Q");
+  return (e && *e ? atoi(e) : 1) && dtype == GH_BF16;
+}
 
 inline size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -468,6 +601,13 @@ LceLayout lce_layout(int64_t N, int64_t D, int64_t V, int64_t chunk, int dtype, 
   // second split-K partial of a chunk's dH [chunk, D]
   L.dh2 = off;
   if (!loss_only) off = al256(off + (size_t)chunk * D * elt);
+  L.q = !loss_only && q_mode_for(dtype);
+  if (L.q) {
+    L.qmode = off;   off = al256(off + (size_t)L.num_n * 2 * chunk);
+    L.alpha = off;   off = al256(off + sizeof(float) * chunk);
+    L.rowflag = off; off = al256(off + sizeof(int) * chunk);
+    L.hs = off;      off = al256(off + (size_t)chunk * D * elt);
+  }
   L.total = off;
   return L;
 }
@@ -510,6 +650,14 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
   float* acc = reinterpret_cast<float*>(ws + L.acc);
   const bool with_grad = grad_input || grad_weight;
   const bool fp32_accum = L.need_acc;
+  // q mode is decided by the layout alone (dtype and GREYHOUND_B200_LCE_Q),
+  // so the calls that continue this one from the workspace agree with it
+  const bool q = L.q && with_grad;
+  const bool q_dw = q && (grad_weight || (flags & GH_LCE_KEEP_DW_OPERAND));
+  uint8_t* qmode = reinterpret_cast<uint8_t*>(ws + L.qmode);
+  float* alpha = reinterpret_cast<float*>(ws + L.alpha);
+  int* rowflag = reinterpret_cast<int*>(ws + L.rowflag);
+  T* hs = reinterpret_cast<T*>(ws + L.hs);
   int rc = GH_OK;
   cudaMemsetAsync(status, 0, sizeof(int), st);
   const float* sp = grad_scale;
@@ -546,18 +694,37 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       p.stats = stats;
       p.xt = xt;
       p.status = status;
+      p.qmode = qmode;
       ProfScope prof(PROF_GEMM_LOGITS_CE, st);
-      rc = launch_gemm_mm<T, gemm::EPI_LCE, T>(ta, tb, 0, 0, pair, nsub, p, sms, st);
+      if (q) rc = launch_gemm_mm<T, gemm::EPI_LCE_Q, T>(ta, tb, 0, 0, pair, 1, p, sms, st);
+      else rc = launch_gemm_mm<T, gemm::EPI_LCE, T>(ta, tb, 0, 0, pair, nsub, p, sms, st);
       if (rc) return rc;
     }
-    // 2. per-row logsumexp and loss terms
+    // 2. per-row logsumexp and loss terms (q mode: also the per-row factor)
     lce_combine_kernel<<<(unsigned)((rows + 31) / 32), 32 * kCombineWarps, 0, st>>>(
-        stats, L.num_n, rows, xt, tc, 0, V, ignore, lse, row_ce + s0, row_z + s0, nullptr, status);
+        stats, L.num_n, rows, xt, tc, 0, V, ignore, lse, row_ce + s0, row_z + s0, nullptr, status,
+        q ? QOut{qmode, sp, zmul, alpha, rowflag} : QOut{nullptr, nullptr, 0.f, nullptr, nullptr});
     count_launch(1);
     if ((rc = check_launch("lce_combine"))) return rc;
     if (!with_grad) continue;
-    // 3. dlogits in place
-    if ((rc = lce_dlogits<T>(logits, L.ldl, tc, lse, rows, V, zmul, ignore, sp, st))) return rc;
+    if (q) {
+      // 3q. rows q mode cannot represent are rewritten (most CTAs return at
+      //     once), the target column of the others gets its one-hot term,
+      //     and H is scaled by alpha for the dW GEMM
+      ProfScope prof(PROF_DLOGITS, st);
+      lce_q_fixup_kernel<T><<<(unsigned)rows, 256, 0, st>>>(logits, L.ldl, qmode, rowflag, lse, tc, 0, rows, V, zmul);
+      lce_q_target_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(logits, L.ldl, tc, xt, lse, rowflag,
+                                                                             alpha, rows, V, ignore, zmul);
+      count_launch(2);
+      if (q_dw) {
+        scale_rows_kernel<T><<<4 * sms, 256, 0, st>>>(Hc, alpha, rows, D, hs);
+        count_launch(1);
+      }
+      if ((rc = check_launch("lce_q_prep"))) return rc;
+    } else {
+      // 3. dlogits in place
+      if ((rc = lce_dlogits<T>(logits, L.ldl, tc, lse, rows, V, zmul, ignore, sp, st))) return rc;
+    }
     // 4. dW[V, D] (+)= dlogits_c^T @ H_c  (row-major [V, D] = the op's [D, V]
     //    gradient as a transposed view, so autograd can hand it to W.grad as is)
     if (grad_weight) {
@@ -577,6 +744,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
         out_dtype = dtype;
         add_same = first ? nullptr : grad_weight;
       }
+      if (q) B = Operand{hs, D, 1};
       if ((rc = run_gemm(dtype, A, B, V, D, rows, out, out_dtype, D, add_f32, add_same, D, nullptr, 1, sms, st,
                          status, PROF_GEMM_DW, kStreamA_KeepB)))
         return rc;
@@ -586,13 +754,14 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       Operand A{logits, L.ldl, 0};
       Operand B{W, D, 1};
       if ((rc = run_gemm(dtype, A, B, rows, D, V, static_cast<T*>(grad_input) + s0 * D, dtype, D, nullptr, nullptr,
-                         0, nullptr, 1, sms, st, status, PROF_GEMM_DH, Hints{}, ws + L.dh2)))
+                         0, nullptr, 1, sms, st, status, PROF_GEMM_DH, Hints{}, ws + L.dh2, q ? alpha : nullptr)))
         return rc;
     }
   }
   ce_finalize_kernel<<<1, 1024, 0, st>>>(row_ce, row_z, target, N, ignore, ce_sum, z_sum, n_valid);
   count_launch(1);
-  return check_launch("lce_finalize");
+  if ((rc = check_launch("lce_finalize"))) return rc;
+  return publish_status(status, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -632,9 +801,11 @@ int shard_stats_run(const void* H, const void* W, const int64_t* target, int64_t
     if (rc) return rc;
   }
   lce_combine_kernel<<<(unsigned)((N + 31) / 32), 32 * kCombineWarps, 0, st>>>(
-      stats, L.num_n, N, xt, target, vstart, Vs, INT64_MIN, nullptr, nullptr, nullptr, stats3, status);
+      stats, L.num_n, N, xt, target, vstart, Vs, INT64_MIN, nullptr, nullptr, nullptr, stats3, status,
+      QOut{nullptr, nullptr, 0.f, nullptr, nullptr});
   count_launch(1);
-  return check_launch("lce_shard_combine");
+  if ((rc = check_launch("lce_shard_combine"))) return rc;
+  return publish_status(status, st);
 }
 
 template <typename T>
@@ -656,7 +827,7 @@ int shard_grads_run(const void* H, const void* W, const int64_t* target, const f
                        nullptr, 0, nullptr, 1, sms, st, status, PROF_GEMM_DH)))
       return rc;
   }
-  return GH_OK;
+  return publish_status(status, st);
 }
 
 }  // namespace
@@ -711,6 +882,7 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
                                     void* stream) {
   if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
   if (N <= 0) return GH_OK;
+  if (!W || !grad_input || !workspace) return set_error(GH_EINVAL, "null pointer argument");
   LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum);
   if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small");
   char* ws = static_cast<char*>(workspace);
@@ -723,12 +895,47 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
   const int elt = elt_size(dtype);
   Operand A{ws + L.logits + (size_t)row_begin * L.ldl * elt, L.ldl, 0};
   Operand B{W, D, 1};
+  // the q-mode decision gh_lce_fwd_bwd made for this workspace: the rows'
+  // factor alpha then multiplies the product
+  const bool q = L.q;
   // each row range has its own rows of the split-K partial buffer, so the two
   // ranges may run concurrently
-  return run_gemm(dtype, A, B, row_end - row_begin, D, V,
-                  static_cast<char*>(grad_input) + (s0 + row_begin) * D * elt, dtype, D, nullptr, nullptr, 0,
-                  nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), reinterpret_cast<int*>(ws + L.status),
-                  PROF_GEMM_DH, Hints{}, ws + L.dh2 + (size_t)row_begin * D * elt);
+  int* status = reinterpret_cast<int*>(ws + L.status);
+  const int rc = run_gemm(dtype, A, B, row_end - row_begin, D, V,
+                          static_cast<char*>(grad_input) + (s0 + row_begin) * D * elt, dtype, D, nullptr, nullptr, 0,
+                          nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), status, PROF_GEMM_DH, Hints{},
+                          ws + L.dh2 + (size_t)row_begin * D * elt,
+                          q ? reinterpret_cast<const float*>(ws + L.alpha) + row_begin : nullptr);
+  return rc ? rc : publish_status(status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, int dtype, int64_t chunk_rows,
+                               int fp32_grad_weight_accum, void* const* band_out, int nbands, int64_t band_rows,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
+  if (N < 0 || D <= 0 || V <= 0) return set_error(GH_EINVAL, "bad shape");
+  if (!H || !band_out || !workspace) return set_error(GH_EINVAL, "null pointer argument");
+  if (nbands <= 0 || nbands > gemm::kMaxPeers || band_rows <= 0 || band_rows % (2 * BM) ||
+      (int64_t)nbands * band_rows < V)
+    return set_error(GH_EINVAL, "need 1..%d bands of a multiple of %d rows covering the vocabulary",
+                     gemm::kMaxPeers, 2 * BM);
+  LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum);
+  if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small");
+  if (N > L.chunk) return set_error(GH_EUNSUPPORTED, "band-stored weight gradient needs all rows in one chunk");
+  if (N == 0) return GH_OK;
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  PeerOut po;
+  po.n = nbands;
+  po.rows = band_rows;
+  for (int i = 0; i < nbands; ++i) po.ptr[i] = band_out[i];
+  // q mode: gh_lce_fwd_bwd(..., GH_LCE_KEEP_DW_OPERAND) left alpha * H in the workspace
+  Operand A{ws + L.logits, L.ldl, 1};
+  Operand B = L.q ? Operand{ws + L.hs, D, 1} : Operand{H, D, 1};
+  int* status = reinterpret_cast<int*>(ws + L.status);
+  const int rc = run_gemm(dtype, A, B, V, D, N, nullptr, dtype, D, nullptr, nullptr, 0, nullptr, 1, num_sms_dev(), st,
+                          status, PROF_GEMM_DW, kStreamA_KeepB, nullptr, nullptr, &po);
+  return rc ? rc : publish_status(status, st);
 }
 
 extern "C" int gh_gemm(const void* A, int64_t lda, int a_mn_major, const void* B, int64_t ldb, int b_mn_major,
@@ -741,8 +948,9 @@ extern "C" int gh_gemm(const void* A, int64_t lda, int a_mn_major, const void* B
   const float* add_f32 = out_dtype == GH_F32 ? static_cast<const float*>(addend) : nullptr;
   const void* add_same = out_dtype == GH_F32 ? nullptr : addend;
   const int raster = M >= N ? 1 : 0;
-  return run_gemm(dtype, a, b, M, N, K, out, out_dtype, ldo, add_f32, add_same, ld_add, scale, raster, 0,
-                  static_cast<cudaStream_t>(stream), status);
+  const int rc = run_gemm(dtype, a, b, M, N, K, out, out_dtype, ldo, add_f32, add_same, ld_add, scale, raster, 0,
+                          static_cast<cudaStream_t>(stream), status);
+  return rc ? rc : publish_status(status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" size_t gh_lce_shard_workspace_bytes(int64_t N, int64_t D, int64_t V_shard, int dtype) {
@@ -798,9 +1006,11 @@ extern "C" int gh_lce_shard_dw(const void* H, int64_t N, int64_t D, int64_t V_sh
   LceLayout L = lce_layout(N, D, V_shard, N, dtype, 0);
   if (workspace_bytes < L.total) return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
   char* ws = static_cast<char*>(workspace);
-  return run_gemm(dtype, Operand{ws + L.logits, L.ldl, 1}, Operand{H, D, 1}, V_shard, D, N, grad_weight_shard, dtype,
-                  D, nullptr, nullptr, 0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream),
-                  reinterpret_cast<int*>(ws + L.status), PROF_GEMM_DW, kStreamA_KeepB);
+  int* status = reinterpret_cast<int*>(ws + L.status);
+  const int rc = run_gemm(dtype, Operand{ws + L.logits, L.ldl, 1}, Operand{H, D, 1}, V_shard, D, N, grad_weight_shard,
+                          dtype, D, nullptr, nullptr, 0, nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream),
+                          status, PROF_GEMM_DW, kStreamA_KeepB);
+  return rc ? rc : publish_status(status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gh_gemm_selftest_stall(void* scratch, size_t scratch_bytes, int* status, int wait_ms, void* stream) {
@@ -823,6 +1033,7 @@ extern "C" int gh_gemm_selftest_stall(void* scratch, size_t scratch_bytes, int* 
   p.status = status;
   p.wait_limit_ns = (uint64_t)wait_ms * 1000000ull;
   p.debug_no_loads = 1;
-  return launch_gemm_t<__nv_bfloat16, 0, 0, gemm::EPI_STORE, __nv_bfloat16, 1>(ta, tb, p, 1,
-                                                                              static_cast<cudaStream_t>(stream));
+  rc = launch_gemm_t<__nv_bfloat16, 0, 0, gemm::EPI_STORE, __nv_bfloat16, 1>(ta, tb, p, 1,
+                                                                           static_cast<cudaStream_t>(stream));
+  return rc ? rc : publish_status(status, static_cast<cudaStream_t>(stream));
 }

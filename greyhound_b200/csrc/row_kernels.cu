@@ -426,12 +426,12 @@ extern "C" size_t gh_sls_workspace_bytes(int64_t rows, int64_t vocab, int dtype)
   return gh_ce_workspace_bytes(rows, vocab, dtype);
 }
 
-extern "C" int gh_ce_fwd_grad(const void* logits, void* dlogits, const int64_t* labels,
-                              int64_t rows, int64_t vocab, int dtype, float z_loss_multiplier,
-                              int64_t ignore_index, int mean_reduction,
-                              const float* grad_scale, float* ce_sum, float* z_sum,
-                              float* n_valid, float* lse_out, void* workspace, size_t workspace_bytes,
-                              void* stream) {
+// publish: end with publish_status (the pinned error slots are allocated on
+// first use, so the allocation-free entry point passes false).
+static int ce_fwd_grad_impl(const void* logits, void* dlogits, const int64_t* labels, int64_t rows, int64_t vocab,
+                            int dtype, float z_loss_multiplier, int64_t ignore_index, int mean_reduction,
+                            const float* grad_scale, float* ce_sum, float* z_sum, float* n_valid, float* lse_out,
+                            void* workspace, size_t workspace_bytes, void* stream, bool publish) {
   if (!is_float_dtype(dtype)) return set_error(GH_ETYPE, "unsupported logits dtype code %d", dtype);
   if (rows < 0 || vocab <= 0) return set_error(GH_EINVAL, "bad shape rows=%lld vocab=%lld",
                                                 (long long)rows, (long long)vocab);
@@ -447,17 +447,34 @@ extern "C" int gh_ce_fwd_grad(const void* logits, void* dlogits, const int64_t* 
   if (!p.fused && rows > 65535) p.fused = true;  // grid.y limit; unreachable by plan_rows
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
+  int rc;
   switch (dtype) {
     case GH_BF16:
-      return launch_ce<__nv_bfloat16>(logits, dlogits, labels, rows, vocab, z_loss_multiplier,
-                                      ignore_index, mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, ws, p, w, st);
+      rc = launch_ce<__nv_bfloat16>(logits, dlogits, labels, rows, vocab, z_loss_multiplier, ignore_index,
+                                    mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, ws, p, w, st);
+      break;
     case GH_F16:
-      return launch_ce<__half>(logits, dlogits, labels, rows, vocab, z_loss_multiplier,
-                               ignore_index, mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, ws, p, w, st);
+      rc = launch_ce<__half>(logits, dlogits, labels, rows, vocab, z_loss_multiplier, ignore_index, mean_reduction,
+                             grad_scale, ce_sum, z_sum, n_valid, lse_out, ws, p, w, st);
+      break;
     default:
-      return launch_ce<float>(logits, dlogits, labels, rows, vocab, z_loss_multiplier,
-                              ignore_index, mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, ws, p, w, st);
+      rc = launch_ce<float>(logits, dlogits, labels, rows, vocab, z_loss_multiplier, ignore_index, mean_reduction,
+                            grad_scale, ce_sum, z_sum, n_valid, lse_out, ws, p, w, st);
+      break;
   }
+  if (rc || !publish) return rc;
+  return publish_status(reinterpret_cast<int*>(ws + w.status), st);
+}
+
+extern "C" int gh_ce_fwd_grad(const void* logits, void* dlogits, const int64_t* labels,
+                              int64_t rows, int64_t vocab, int dtype, float z_loss_multiplier,
+                              int64_t ignore_index, int mean_reduction,
+                              const float* grad_scale, float* ce_sum, float* z_sum,
+                              float* n_valid, float* lse_out, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  return ce_fwd_grad_impl(logits, dlogits, labels, rows, vocab, dtype, z_loss_multiplier, ignore_index,
+                          mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, workspace, workspace_bytes,
+                          stream, true);
 }
 
 template <typename T, typename I>
@@ -497,11 +514,13 @@ extern "C" int gh_sls_fwd(const void* logits, const void* index, int index_dtype
     return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, w.total);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
+  int rc;
   switch (dtype) {
-    case GH_BF16: return sls_dispatch_idx<__nv_bfloat16>(logits, index, index_dtype, rows, vocab, out, out_dtype, lse_out, ws, p, w, st);
-    case GH_F16: return sls_dispatch_idx<__half>(logits, index, index_dtype, rows, vocab, out, out_dtype, lse_out, ws, p, w, st);
-    default: return sls_dispatch_idx<float>(logits, index, index_dtype, rows, vocab, out, out_dtype, lse_out, ws, p, w, st);
+    case GH_BF16: rc = sls_dispatch_idx<__nv_bfloat16>(logits, index, index_dtype, rows, vocab, out, out_dtype, lse_out, ws, p, w, st); break;
+    case GH_F16: rc = sls_dispatch_idx<__half>(logits, index, index_dtype, rows, vocab, out, out_dtype, lse_out, ws, p, w, st); break;
+    default: rc = sls_dispatch_idx<float>(logits, index, index_dtype, rows, vocab, out, out_dtype, lse_out, ws, p, w, st); break;
   }
+  return rc ? rc : publish_status(reinterpret_cast<int*>(ws + w.status), st);
 }
 
 template <typename T, typename I>
@@ -658,14 +677,27 @@ extern "C" int gh_ce_fwd_grad_noalloc(const void* logits, void* dlogits, const i
   if (need == 0 && (!is_float_dtype(dtype)))
     return set_error(GH_ETYPE, "unsupported logits dtype code %d", dtype);
   if (need > kNoAllocScratchBytes)
-    return set_error(GH_EINVAL,
+    return set_error(GH_EWORKSPACE,
                      "gh_ce_fwd_grad_noalloc: %lld rows x %lld vocab need %zu scratch bytes, more than the "
                      "fixed %zu; use gh_ce_fwd_grad with a caller workspace",
                      (long long)rows, (long long)vocab, need, kNoAllocScratchBytes);
   void* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
-  return gh_ce_fwd_grad(logits, dlogits, labels, rows, vocab, dtype, z_loss_multiplier, ignore_index,
-                        mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, scratch,
-                        kNoAllocScratchBytes, stream);
+  return ce_fwd_grad_impl(logits, dlogits, labels, rows, vocab, dtype, z_loss_multiplier, ignore_index,
+                          mean_reduction, grad_scale, ce_sum, z_sum, n_valid, lse_out, scratch,
+                          kNoAllocScratchBytes, stream, false);
+}
+
+extern "C" int gh_ce_noalloc_status(int* host_out, void* stream) {
+  if (!host_out) return set_error(GH_EINVAL, "null pointer argument");
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  // the status word sits at offset 0 of the shared scratch (as in any workspace)
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(host_out, scratch, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return set_error(GH_ECUDA, "gh_ce_noalloc_status: %s", cudaGetErrorString(e));
+  return GH_OK;
 }

@@ -48,7 +48,18 @@ constexpr int EPI_WARPS = 8;
 constexpr int EPI_CHUNKS = BN / 32 / (EPI_WARPS / 4);  // 32-column chunks per warp per half
 constexpr int TMEM_COLS = 2 * BN;
 
-enum Epi { EPI_STORE = 0, EPI_LCE = 1 };
+enum Epi { EPI_STORE = 0, EPI_LCE = 1, EPI_LCE_Q = 2 };
+constexpr int kMaxPeers = 8;
+
+// Exponent window of the unnormalised-probability store (EPI_LCE_Q), in log2
+// units: a row group whose largest logit x satisfies
+// kQLo <= x * log2(e) <= kQHi stores q = 2^(x log2 e) = e^x (at most 2^80,
+// so sums over the vocabulary and the dH accumulator stay far inside fp32,
+// and the largest term is far above bf16's smallest normal). Other groups
+// store the raw logits and are rewritten by a fix-up pass once the row's
+// logsumexp is known.
+constexpr float kQHi = 80.f;
+constexpr float kQLo = -80.f;
 
 struct Params {
   int M, N, K;
@@ -74,6 +85,19 @@ struct Params {
   float2* stats;          // [num_n][M] (max, sum-exp) in log2 units
   float* xt;              // [M] target logit (written by the tile holding it)
   int* status;            // device error word (bit 2: pipeline timeout)
+  // EPI_LCE_Q: per (256-column tile, 128-column group, row) byte, 1 when
+  // that group of the row holds raw logits instead of q ([num_n][2][M])
+  uint8_t* qmode;
+  // EPI_STORE: optional per-row factor multiplying the product ([M] fp32)
+  const float* row_scale;
+  // EPI_STORE, 16-bit output: when npeer > 0 the output rows are split into
+  // bands of peer_rows rows (a multiple of the tile height) and band b is
+  // stored at peer_out[b] (row r at peer_out[b] + (r - b * peer_rows) * ldo),
+  // which may be another GPU's memory: the GEMM's tiles go straight to the
+  // rank that reduces that band (a reduce-scatter fused into the epilogue).
+  int npeer;
+  int64_t peer_rows;
+  void* peer_out[kMaxPeers];
   // L2 policy of each operand's TMA loads (0 none, 1 evict_first, 2 evict_last)
   // and of the epilogue stores (1: evict_first for a large streamed output)
   int a_hint, b_hint, out_evict_first;
@@ -83,6 +107,16 @@ struct Params {
   uint64_t wait_limit_ns;
   int debug_no_loads;
 };
+
+// Output base of the tile whose first row is m0: the band owner's buffer,
+// offset so that indexing it with the global row lands in that band.
+template <typename OutT>
+__device__ __forceinline__ OutT* tile_out_base(const Params& p, void* pout, int m0) {
+  if (p.npeer <= 0) return reinterpret_cast<OutT*>(pout);
+  int b = (int)(m0 / p.peer_rows);
+  if (b >= p.npeer) b = p.npeer - 1;
+  return reinterpret_cast<OutT*>(p.peer_out[b]) - (int64_t)b * p.peer_rows * p.ldo;
+}
 
 // Tile order. The grouped orders bound how much of the re-read operand is live
 // at once (a group of m-tiles shares one pass over all n-tiles), so it stays
@@ -310,6 +344,27 @@ __device__ __forceinline__ void lce_fold16(const float (&x)[16], bool full, int 
   m_run = mnew;
 }
 
+// If the target column (lab_rel, relative to the 256-column half) lies in
+// 32-column chunk c, write its 16-bit logit (from the packed words w) to *xt_row.
+template <typename OutT>
+__device__ __forceinline__ void lce_target_from_chunk(const uint32_t* w, int c, int64_t lab_rel, float* xt_row) {
+  const int64_t li = lab_rel - c * 32;
+  if ((uint64_t)li < 32u) {
+    // one select per word, written so the compiler cannot turn the chain
+    // into an indexed load (that would move w to local memory)
+    uint32_t word = 0;
+    const int wi = (int)(li >> 1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\tselp.b32 %0, %1, %0, p;\n\t}"
+          : "+r"(word)
+          : "r"(w[j]), "r"(wi), "r"(j));
+    float lo, hi;
+    unpack2<OutT>(word, lo, hi);
+    *xt_row = (li & 1) ? hi : lo;
+  }
+}
+
 // Fold 32 packed 16-bit logits (columns c * 32 .. c * 32 + 31 of a 256-column
 // half starting at n0) into the running pair and record the target logit if
 // it lies in this chunk (lab_rel: target column relative to n0). Two
@@ -326,21 +381,7 @@ __device__ __forceinline__ void lce_fold_chunk(const uint32_t* w, int c, int n0,
     for (int j = 0; j < 8; ++j) unpack2<OutT>(w[sc * 8 + j], x[2 * j], x[2 * j + 1]);
     lce_fold16(x, full, col0 + sc * 16, N, m_run, s_run);
   }
-  const int64_t li = lab_rel - c * 32;
-  if ((uint64_t)li < 32u) {
-    // one select per word, written so the compiler cannot turn the chain
-    // into an indexed load (that would move w to local memory)
-    uint32_t word = 0;
-    const int wi = (int)(li >> 1);
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      asm("{\n\t.reg .pred p;\n\tsetp.eq.s32 p, %2, %3;\n\tselp.b32 %0, %1, %0, p;\n\t}"
-          : "+r"(word)
-          : "r"(w[j]), "r"(wi), "r"(j));
-    float lo, hi;
-    unpack2<OutT>(word, lo, hi);
-    *xt_row = (li & 1) ? hi : lo;
-  }
+  lce_target_from_chunk<OutT>(w, c, lab_rel, xt_row);
 }
 
 // Geometry of one configuration. PAIR = 1: one CTA computes a 128 x 256 tile.
@@ -376,6 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   using G = Geo<PAIR, NSUB>;
   static_assert(NSUB == 1 || sizeof(OutT) == 2, "the 512-column tile parks 16-bit outputs only");
+  static_assert(EPI != EPI_LCE_Q || NSUB == 1, "the q store runs on 256-column tiles");
   constexpr int STG = G::STG;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -662,10 +704,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           constexpr int PW = (EPI_CHUNKS - 1) * 16;  // parked words per half
           uint32_t pk[2][PW];
           float hm[2] = {kNegInf, kNegInf}, hs[2] = {0.f, 0.f};
-          const float scale = (EPI == EPI_STORE && p.scale) ? *p.scale : 1.f;
+          const float scale = (EPI == EPI_STORE && p.scale ? *p.scale : 1.f) *
+                              (EPI == EPI_STORE && p.row_scale && row_ok ? p.row_scale[row] : 1.f);
           const int64_t lab = (EPI == EPI_LCE && row_ok) ? p.labels[row] - p.label_offset : -1;
           float* xt_row = EPI == EPI_LCE ? p.xt + row : nullptr;
-          OutT* out = reinterpret_cast<OutT*>(pout);
+          OutT* out = tile_out_base<OutT>(p, pout, mt * G::TM);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             if (!tc::mbar_wait(&tfull[h], acc_phase, abort_flag, lim)) { stop = true; break; }
@@ -735,7 +778,85 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + sub * BN + c0 * 32;
         if (n0 < p.N) {
           __syncwarp();
-          if constexpr (EPI == EPI_LCE) {
+          if constexpr (EPI == EPI_LCE_Q) {
+            static_assert(NSUB == 1 && sizeof(OutT) == 2, "the q store runs on 256-column tiles, 16-bit output");
+            const int64_t lab = row_ok ? p.labels[row] - p.label_offset : -1;
+            const int64_t lab_rel = lab - n0;
+            // Pass 1: the window decision for this row's 128 columns of the
+            // tile, from the fp32 accumulator.
+            float cmax = kNegInf;
+#pragma unroll 1
+            for (int i = 0; i < EPI_CHUNKS; ++i) {
+              uint32_t r[32];
+              tc::tmem_ld32(tbase + i * 32, r);
+              tc::tmem_ld_wait(r);
+              const int col0 = n0 + (c0 + i) * 32;
+              if (col0 + 32 <= p.N) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) cmax = fmaxf(cmax, __uint_as_float(r[j]));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < p.N) cmax = fmaxf(cmax, __uint_as_float(r[j]));
+              }
+            }
+            const bool any_col = n0 + c0 * 32 < p.N;
+            const float cml = cmax * kLog2e;
+            const bool raw = any_col && !(cml <= kQHi && cml >= kQLo);  // NaN: raw
+            if (row_ok && any_col) p.qmode[((int64_t)(nt * NSUB + h) * 2 + g) * p.M + row] = raw ? 1 : 0;
+            // Pass 2: round to bf16 (the reference's logits dtype), record the
+            // target logit, then store q = e^x (or the raw logit) and fold the
+            // statistics: sum q directly (pair (0, sum)) or, for raw groups,
+            // the running (max, sum) of the plain CE epilogue.
+            float m_run = kNegInf, s_run = 0.f, s_q = 0.f;
+#pragma unroll 1
+            for (int i = 0; i < EPI_CHUNKS; ++i) {
+              const int c = c0 + i;
+              const int col0 = n0 + c * 32;
+              uint32_t w[16];
+#pragma unroll
+              for (int sc = 0; sc < 2; ++sc) {
+                uint32_t r[16];
+                tc::tmem_ld16_wait(tbase + i * 32 + sc * 16, r);
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  w[sc * 8 + j] = pack2<OutT>(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              }
+              lce_target_from_chunk<OutT>(w, c, lab_rel, p.xt + row);
+              const bool full = col0 + 32 <= p.N;
+              if (raw) {
+#pragma unroll
+                for (int sc = 0; sc < 2; ++sc) {
+                  float x[16];
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) unpack2<OutT>(w[sc * 8 + j], x[2 * j], x[2 * j + 1]);
+                  lce_fold16(x, full, col0 + sc * 16, p.N, m_run, s_run);
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  float a, b;
+                  unpack2<OutT>(w[j], a, b);
+                  a = fast_exp2(a * kLog2e);
+                  b = fast_exp2(b * kLog2e);
+                  if (!full) {
+                    if (col0 + 2 * j >= p.N) a = 0.f;
+                    if (col0 + 2 * j + 1 >= p.N) b = 0.f;
+                  }
+                  s_q += a + b;
+                  w[j] = pack2<OutT>(a, b);
+                }
+              }
+              if (pout)
+                store_chunk_packed<OutT>(reinterpret_cast<OutT*>(pout), p.ldo, m0 + q * 32, p.M, col0, p.N, w,
+                                         stage_out, lane, p.vec_ok, p.out_evict_first);
+            }
+            if (!raw) {
+              m_run = s_q > 0.f ? 0.f : kNegInf;
+              s_run = s_q;
+            }
+            if (!stats_exchange_at(h, m_run, s_run)) stop = true;
+          } else if constexpr (EPI == EPI_LCE) {
             const int64_t lab = row_ok ? p.labels[row] - p.label_offset : -1;
             const int64_t lab_rel = lab - n0;  // label column inside this half, if any
             float m_run = kNegInf, s_run = 0.f;
@@ -761,7 +882,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             // group 1 hands its (max, sum) to group 0, which writes the half's stats
             if (!stats_exchange_at(h, m_run, s_run)) stop = true;
           } else {
-            const float scale = p.scale ? *p.scale : 1.f;
+            const float scale = (p.scale ? *p.scale : 1.f) * (p.row_scale && row_ok ? p.row_scale[row] : 1.f);
             uint32_t ra[32], rb[32];
             tc::tmem_ld32(tbase, ra);
 #pragma unroll
@@ -787,8 +908,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
                   for (int j = 0; j < 32; ++j) v[j] += a[j];
                 }
-                store_chunk<OutT>(reinterpret_cast<OutT*>(pout), p.ldo, m0 + q * 32, p.M, col0, p.N, v, stage_out,
-                                  lane, p.vec_ok, p.out_evict_first);
+                store_chunk<OutT>(tile_out_base<OutT>(p, pout, mt * G::TM), p.ldo, m0 + q * 32, p.M, col0, p.N, v,
+                                  stage_out, lane, p.vec_ok, p.out_evict_first);
               }
             }
           }
@@ -806,6 +927,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       }
     }
   }
+  // stores to another GPU's memory are visible there before the grid is done
+  if (p.npeer > 0 && warp >= EPI_WARP0) __threadfence_system();
   __syncthreads();
   if (PAIR == 2) tc::cluster_sync();  // no CTA leaves while its peer may still signal it
   if (threadIdx.x == 0 && *abort_flag && p.status) atomicOr(p.status, 4);

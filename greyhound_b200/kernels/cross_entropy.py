@@ -61,6 +61,7 @@ def cross_entropy_with_grad(
         raise ValueError("expected non-empty vocabulary dimension")
     lib = _lib.load()
     dev = logits.device
+    _lib.raise_pending(dev, "cross_entropy_with_grad")
     # Three separate 0-d tensors, like the reference (outputs never alias).
     ce_sum = torch.empty((), dtype=torch.float32, device=dev)
     z_sum = torch.empty((), dtype=torch.float32, device=dev)

@@ -88,6 +88,7 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
     dev = inputs.device
     chunk = chunk_size_for(B, D, V, inputs.element_size())
     lib = _lib.load()
+    _lib.raise_pending(dev, "linear_cross_entropy")
     code = _lib.dtype_code(inputs.dtype)
     if with_grad:
         ws_bytes = lib.gh_lce_workspace_bytes(B, D, V, chunk, code, int(fp32_accum))
@@ -261,6 +262,7 @@ def vocab_shard_stats(
         x = inputs.contiguous()
         w = weight_shard.contiguous()
         lib = _lib.load()
+        _lib.raise_pending(dev, "vocab_shard_stats")
         code = _lib.dtype_code(inputs.dtype)
         ws = _lib.workspace(lib.gh_lce_shard_workspace_bytes(rows, D, Vs, code), dev)
         stats = torch.empty((rows, 3), dtype=torch.float32, device=dev)
@@ -311,6 +313,7 @@ def vocab_shard_grads(
     lse = lse.contiguous().float()
     sc = scale.reshape(1).float().contiguous()
     lib = _lib.load()
+    _lib.raise_pending(dev, "vocab_shard_grads")
     if state[0] == "tc":
         _, ws, x, w = state
         gi = torch.empty((rows, D), dtype=inputs.dtype, device=dev)

@@ -54,6 +54,7 @@ def selective_log_softmax_with_lse(
     out = torch.empty(index.shape, dtype=out_dtype, device=logits.device)
     lse = torch.empty(index.shape, dtype=torch.float32, device=logits.device) if want_lse else None
     lib = _lib.load()
+    _lib.raise_pending(logits.device, "selective_log_softmax")
     code = _lib.dtype_code(logits.dtype)
     ws = _lib.workspace(lib.gh_sls_workspace_bytes(rows, vocab, code), logits.device)
     status = lib.gh_sls_fwd(
@@ -103,6 +104,7 @@ def selective_log_softmax_backward_kernel(
         grad_out = grad_out.float()
     grad = torch.empty_like(logits)
     lib = _lib.load()
+    _lib.raise_pending(logits.device, "selective_log_softmax_backward")
     status = lib.gh_sls_bwd(
         logits.data_ptr(),
         index.data_ptr(),

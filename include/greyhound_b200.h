@@ -14,7 +14,9 @@
  *   - the library never allocates device memory: scratch space is passed in
  *     by the caller (`workspace`, sized by the matching *_workspace_bytes);
  *   - device-side problems (e.g. a label outside [0, V)) never trap: they are
- *     recorded in the workspace status word, see gh_workspace_status_offset().
+ *     recorded in the workspace status word, see gh_workspace_status_offset(),
+ *     and every entry point with a workspace ends by OR-ing that word into a
+ *     per-device sticky slot in pinned host memory (gh_take_device_errors).
  */
 #ifndef GREYHOUND_B200_H
 #define GREYHOUND_B200_H
@@ -63,6 +65,15 @@ GH_API const char* gh_last_error_string(void);
 GH_API long long gh_launch_count(void);
 /* Byte offset of the int32 device status word inside any workspace. */
 GH_API size_t gh_workspace_status_offset(void);
+/* Returns and clears the GH_DEV_* bits that calls on `device` have recorded
+ * since the last call of this function (no counterpart in the reference,
+ * whose kernels raise ValueError for bad labels on the host before launch,
+ * src/greyhound/kernels/cross_entropy.py:173-184; here labels are checked on
+ * the device, so the check costs no host sync). Never synchronises: bits of
+ * a call that the GPU has not run yet are not visible. The first entry point
+ * called in a process allocates the small pinned host array behind these
+ * slots (cudaHostAlloc); make that call before any stream capture. */
+GH_API int gh_take_device_errors(int device);
 
 /* ------------------------------------------------------------------------ *
  * Standalone cross-entropy with logits gradient.
@@ -100,11 +111,14 @@ GH_API int gh_ce_fwd_grad(const void* logits, void* dlogits, const int64_t* labe
  * without a device allocator): the scratch is a fixed library-owned device
  * array of gh_ce_noalloc_scratch_bytes() (4 MiB) that every GPU loading the
  * library holds until exit. Shapes whose scratch would exceed it are rejected
- * with GH_EINVAL (about 349,000 rows at any vocab size). The first call on a
+ * (about 349,000 rows at any vocab size). The first call on a
  * device looks up the array's device address (make it before any stream
  * capture). All calls share the array, so calls that overlap on the GPU
  * (concurrent streams) race; serialise them. Arguments and results as
- * gh_ce_fwd_grad. */
+ * gh_ce_fwd_grad, except: a shape too large for the array returns
+ * GH_EWORKSPACE (the code gh_ce_fwd_grad gives a too-small workspace), and
+ * the device status word is not published to gh_take_device_errors (that
+ * would allocate); read it with gh_ce_noalloc_status. */
 GH_API size_t gh_ce_noalloc_scratch_bytes(void);
 GH_API int gh_ce_fwd_grad_noalloc(const void* logits, void* dlogits, const int64_t* labels,
                                   int64_t rows, int64_t vocab, int dtype,
@@ -112,6 +126,9 @@ GH_API int gh_ce_fwd_grad_noalloc(const void* logits, void* dlogits, const int64
                                   int mean_reduction, const float* grad_scale,
                                   float* ce_sum, float* z_sum, float* n_valid, float* lse_out,
                                   void* stream);
+/* The GH_DEV_* status bits of the last gh_ce_fwd_grad_noalloc call on this
+ * device, copied to *host_out (a host int). Synchronises `stream`. */
+GH_API int gh_ce_noalloc_status(int* host_out, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Selective log-softmax: out[r] = logits[r, index[r]] - logsumexp(logits[r]).
@@ -174,10 +191,12 @@ GH_API int gh_logits_grad(const void* logits, void* dlogits, const int64_t* labe
  *          into the logits gradient, so both gradients come out scaled
  *   flags: GH_LCE_DEFER_LAST_DH -> the last chunk's grad_input rows are not
  *          computed; call gh_lce_dh_last_chunk later (lets a data-parallel
- *          caller start the grad_weight all-reduce first)
+ *          caller start the grad_weight all-reduce first);
+ *          GH_LCE_KEEP_DW_OPERAND with grad_weight == NULL -> leave the weight
+ *          gradient's operands in the workspace for gh_lce_dw_peers
  *   ce_sum, z_sum, n_valid: float scalars (overwritten)
  * ------------------------------------------------------------------------ */
-enum { GH_LCE_DEFER_LAST_DH = 1 };
+enum { GH_LCE_DEFER_LAST_DH = 1, GH_LCE_KEEP_DW_OPERAND = 2 };
 
 GH_API size_t gh_lce_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows,
                                      int dtype, int fp32_grad_weight_accum);
@@ -195,14 +214,46 @@ GH_API int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target,
                           float* ce_sum, float* z_sum, float* n_valid,
                           void* workspace, size_t workspace_bytes, void* stream);
 /* grad_input rows [row_begin, row_end) of the last chunk (offsets inside the
- * chunk; row_end < 0: to the end), from the dlogits left in the workspace by
- * gh_lce_fwd_bwd(..., GH_LCE_DEFER_LAST_DH). max_ctas <= 0: all SMs; fewer
- * leave SMs to a concurrently running collective. */
+ * chunk; row_end < 0: to the end), from what gh_lce_fwd_bwd(...,
+ * GH_LCE_DEFER_LAST_DH) left in the workspace. max_ctas <= 0: all SMs;
+ * fewer leave SMs to a concurrently running collective. */
 GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype,
                                 int64_t chunk_rows, int fp32_grad_weight_accum,
                                 int64_t row_begin, int64_t row_end,
                                 void* grad_input, void* workspace, size_t workspace_bytes,
                                 int max_ctas, void* stream);
+
+/* Weight gradient of a single-chunk call (N <= chunk rows) whose
+ * gh_lce_fwd_bwd ran with grad_weight == NULL and GH_LCE_KEEP_DW_OPERAND,
+ * stored in row bands: rows [b * band_rows, (b + 1) * band_rows) of the
+ * [V, D] gradient go to band_out[b] (row-major, pitch D), b < nbands <= 8,
+ * band_rows a multiple of 256. band_out[b] may point into another GPU's
+ * memory (a CUDA IPC mapping): the data-parallel caller gives each rank's
+ * receive slot, so the GEMM's epilogue performs the scatter of a
+ * reduce-scatter of the weight gradient (no counterpart in the reference,
+ * which is single-device). The kernel ends with a system-scope fence, so
+ * once it has completed the stores are visible to the owners. */
+GH_API int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, int dtype,
+                           int64_t chunk_rows, int fp32_grad_weight_accum,
+                           void* const* band_out, int nbands, int64_t band_rows,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* out0[r, c] (and out1[r, c] when out1 != NULL) = sum over s < nslots of
+ * slots[s * slot_stride + r * ld + c], summed in fp32 in slot order and
+ * rounded once (deterministic): the reduction step of that reduce-scatter.
+ * dtype F16 or BF16; all pointers and ld 16-byte aligned. */
+GH_API int gh_sum_slots(const void* slots, int nslots, int64_t slot_stride, int64_t rows, int64_t cols,
+                        int64_t ld, int dtype, void* out0, void* out1, void* stream);
+
+/* CUDA IPC of a device buffer that need not start its allocation:
+ * gh_ipc_get_handle writes the 64-byte handle of the allocation holding ptr
+ * and ptr's byte offset in it; gh_ipc_open maps a handle from another
+ * process on this node into the current device (peer access enabled) and
+ * returns the mapped base + offset; gh_ipc_close unmaps (give the pointer
+ * and offset gh_ipc_open used). */
+GH_API int gh_ipc_get_handle(const void* ptr, void* handle_out, size_t* offset_out);
+GH_API int gh_ipc_open(const void* handle, size_t offset, void** ptr_out);
+GH_API int gh_ipc_close(void* ptr, size_t offset);
 
 /* ------------------------------------------------------------------------ *
  * Vocab-parallel linear cross-entropy (no counterpart in the reference, which

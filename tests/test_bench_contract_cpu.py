@@ -1,4 +1,4 @@
-"""The reference arm of bench.py (the oracle port on host cores) prints one
+"""The reference arm of bench.py (the reference torch path on host cores) prints one
 JSON line with the keys the driver reads; checked here at a tiny shape."""
 
 import json
@@ -12,7 +12,7 @@ ROOT = Path(__file__).resolve().parent.parent
 def test_reference_arm_prints_the_contract_line():
     res = subprocess.run(
         [sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "3",
-         "--ref-step-seconds", "0.2", "--rows", "64", "--hidden", "128", "--vocab", "1000"],
+         "--ref-rows", "32", "--rows", "64", "--hidden", "128", "--vocab", "1000"],
         cwd=ROOT, capture_output=True, text=True, timeout=300,
     )
     assert res.returncode == 0, res.stderr[-2000:]
