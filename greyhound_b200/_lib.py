@@ -86,6 +86,7 @@ SIGNATURES: dict[str, tuple] = {
     "gh_ipc_get_handle": (_i32, [_vp, _vp, ctypes.POINTER(_sz)]),
     "gh_ipc_open": (_i32, [_vp, _sz, ctypes.POINTER(_vp)]),
     "gh_ipc_close": (_i32, [_vp, _sz]),
+    "gh_memcpy_async": (_i32, [_vp, _vp, _sz, _vp]),
     "gh_take_device_errors": (_i32, [_i32]),
     "gh_ce_noalloc_status": (_i32, [ctypes.POINTER(ctypes.c_int), _vp]),
     "gh_profile_enable": (None, [_i32]),

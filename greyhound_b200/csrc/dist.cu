@@ -126,3 +126,11 @@ extern "C" int gh_ipc_close(void* ptr, size_t offset) {
   if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
   return GH_OK;
 }
+
+extern "C" int gh_memcpy_async(void* dst, const void* src, size_t bytes, void* stream) {
+  if (bytes == 0) return GH_OK;
+  if (!dst || !src) return set_error(GH_EINVAL, "null pointer argument");
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(GH_ECUDA, "cudaMemcpyAsync: %s", cudaGetErrorString(e));
+  return GH_OK;
+}

@@ -10,8 +10,12 @@ all valid tokens of all ranks, divided by the *global* valid-token count for
 * Row sharding (``RowShardedLinearCrossEntropy``): each rank holds its own rows
   of ``inputs``/``target`` and a replica of ``weight``. One scalar all-reduce
   gives the global valid count before any gradient is written, so the
-  ``1 / n_global`` scale is folded into the logits gradient; the weight
-  gradient is then summed across ranks with one all-reduce.
+  ``1 / n_global`` scale is folded into the logits gradient. The weight
+  gradient is summed across ranks by a reduce-scatter fused into the dW
+  GEMM (tiles stored into the owning rank's buffer through CUDA IPC), a
+  fixed-order sum on each owner and copy-engine copies of the reduced bands
+  (``_row_sharded_band_exchange``); an NCCL all-reduce is the fallback for
+  shapes that path does not take (several chunks, fp32, more than 8 ranks).
 * Vocab sharding (``VocabShardedLinearCrossEntropy``): each rank holds rows
   ``[r*V/P, (r+1)*V/P)`` of ``weight`` and all rows of ``inputs``. Per row the
   ranks exchange (max, sum-exp, target-logit) with one all-gather, combine them
@@ -59,11 +63,171 @@ def _global_scale(target: Tensor, ignore_index: int, reduction: str, group) -> t
     return n.reshape(()), scale
 
 
+def _band_rows(V: int, world: int) -> int:
+    """Rows per weight-gradient band: ceil(V / world) rounded up to the GEMM
+    tile height (256)."""
+    per_rank = -(-V // world)
+    return -(-per_rank // 256) * 256
+
+
+class _BandExchange:
+    """Receive buffers of the weight-gradient reduce-scatter that the dW GEMM
+    performs in its epilogue, shared between the ranks of one node with CUDA
+    IPC (allocated once per group / device / shape and kept).
+
+    The ``[V, D]`` gradient is cut into ``world`` row bands of ``band_rows``
+    rows (a multiple of the GEMM tile height). Rank ``b`` owns band ``b``:
+    ``recv[s]`` receives rank ``s``'s partial of that band (written by rank
+    ``s``'s GEMM epilogue through the IPC mapping), and ``shard`` holds the
+    reduced band, which the other ranks copy (copy engines, over NVLink)."""
+
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, group, device, V, D, dtype):
+        key = (id(group), device.index, V, D, dtype)
+        ex = cls._cache.get(key)
+        if ex is None:
+            ex = cls(group, device, V, D, dtype)
+            cls._cache[key] = ex
+        return ex
+
+    def __init__(self, group, device, V, D, dtype):
+        import ctypes
+
+        from greyhound_b200 import _lib
+
+        self.lib = _lib.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.V, self.D, self.dtype = V, D, dtype
+        self.band_rows = _band_rows(V, self.world)
+        # one allocation (one IPC handle): world receive slots, then the reduced band
+        self.buf = torch.empty((self.world + 1, self.band_rows, D), dtype=dtype, device=device)
+        self.recv = self.buf[: self.world]
+        self.shard = self.buf[self.world]
+        h = ctypes.create_string_buffer(64)
+        off = ctypes.c_size_t(0)
+        _lib.check(self.lib.gh_ipc_get_handle(self.buf.data_ptr(), h, ctypes.byref(off)), "gh_ipc_get_handle")
+        allh = [None] * self.world
+        dist.all_gather_object(allh, (h.raw, off.value), group=group)
+        slot = self.band_rows * D * self.buf.element_size()
+        self.opened = []
+        self.band_out = (ctypes.c_void_p * self.world)()
+        self.shard_src = [0] * self.world
+        for r, (hr, orr) in enumerate(allh):
+            if r == self.rank:
+                base = self.buf.data_ptr()
+            else:
+                pr = ctypes.c_void_p()
+                _lib.check(self.lib.gh_ipc_open(hr, orr, ctypes.byref(pr)), "gh_ipc_open")
+                self.opened.append((pr.value, orr))
+                base = pr.value
+            self.band_out[r] = base + self.rank * slot  # this rank's slot in rank r's receive buffer
+            self.shard_src[r] = base + self.world * slot  # rank r's reduced band
+        self.flag = torch.zeros(1, dtype=torch.float32, device=device)
+        self.copy_stream = torch.cuda.Stream(device=device)
+
+    def rows_of(self, b: int) -> int:
+        return min(self.band_rows, self.V - b * self.band_rows)
+
+    def barrier(self):
+        """Stream-ordered barrier: returns on the host at once; the kernels
+        queued after it run once every rank's earlier kernels have finished."""
+        dist.all_reduce(self.flag, group=self.group)
+
+
+def _dp_band_exchange_ok(inputs, weight_dv, world) -> bool:
+    import os
+
+    if os.environ.get("GREYHOUND_B200_DP_PEER", "1") in ("0", ""):
+        return False
+    if not (1 < world <= 8) or not lce._tc_ok(inputs, weight_dv):
+        return False
+    B, D = inputs.shape
+    V = weight_dv.shape[1]
+    return (B > 0 and (world - 1) * _band_rows(V, world) < V
+            and lce.chunk_size_for(B, D, V, inputs.element_size()) >= B)
+
+
+def _row_sharded_band_exchange(inputs, weight_dv, target, ignore_index, z_loss_multiplier, fp32_accum, scale,
+                               group):
+    """Data-parallel step whose weight-gradient all-reduce is a reduce-scatter
+    fused into the dW GEMM's epilogue (each tile stored in the owner rank's
+    receive slot), a fixed-order sum of the slots on each owner, and copies
+    of the reduced bands between the ranks by the copy engines, overlapped
+    with the input-gradient GEMM on all SMs."""
+    from greyhound_b200 import _lib
+
+    B, D = inputs.shape
+    V = weight_dv.shape[1]
+    dev = inputs.device
+    ex = _BandExchange.get(group, dev, V, D, inputs.dtype)
+    lib = ex.lib
+    _lib.raise_pending(dev, "row_sharded_linear_cross_entropy")
+    x = inputs.contiguous()
+    w = lce._weight_vd(weight_dv)
+    t = target.contiguous()
+    code = _lib.dtype_code(inputs.dtype)
+    chunk = lce.chunk_size_for(B, D, V, inputs.element_size())
+    ws = _lib.workspace(lib.gh_lce_workspace_bytes(B, D, V, chunk, code, int(fp32_accum)), dev)
+    ce_sum = torch.empty((), dtype=torch.float32, device=dev)
+    z_sum = torch.empty((), dtype=torch.float32, device=dev)
+    n_valid = torch.empty((), dtype=torch.float32, device=dev)
+    gi = torch.empty((B, D), dtype=inputs.dtype, device=dev)
+    gw = torch.empty((V, D), dtype=inputs.dtype, device=dev)
+    gs = scale.reshape(1).float().contiguous()
+    stream = _lib.stream_of(x)
+    # logits GEMM + statistics + the gradient operands; no dW, dH deferred
+    st = lib.gh_lce_fwd_bwd(
+        x.data_ptr(), w.data_ptr(), t.data_ptr(), B, D, V, code, float(z_loss_multiplier), int(ignore_index), 0,
+        gs.data_ptr(), chunk, int(fp32_accum), _lib.GH_LCE_DEFER_LAST_DH | _lib.GH_LCE_KEEP_DW_OPERAND,
+        gi.data_ptr(), None, ce_sum.data_ptr(), z_sum.data_ptr(), n_valid.data_ptr(), ws.data_ptr(), ws.numel(),
+        stream)
+    _lib.check(st, "linear_cross_entropy")
+    # dW, each band's tiles stored straight into its owner's receive slot
+    st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), ex.band_out, ex.world,
+                             ex.band_rows, ws.data_ptr(), ws.numel(), stream)
+    _lib.check(st, "gh_lce_dw_peers")
+    ex.barrier()  # every rank's slot of my band has arrived
+    me = ex.rank
+    st = lib.gh_sum_slots(ex.recv.data_ptr(), ex.world, ex.band_rows * D, ex.rows_of(me), D, D, code,
+                          ex.shard.data_ptr(), gw[me * ex.band_rows:].data_ptr(), stream)
+    _lib.check(st, "gh_sum_slots")
+    ex.barrier()  # every rank's reduced band is ready
+    ready = torch.cuda.Event()
+    ready.record()
+    cs = ex.copy_stream
+    cs.wait_event(ready)
+    elt = gw.element_size()
+    for r in range(ex.world):
+        if r != me:
+            st = lib.gh_memcpy_async(gw[r * ex.band_rows:].data_ptr(), ex.shard_src[r], ex.rows_of(r) * D * elt,
+                                     cs.cuda_stream)
+            _lib.check(st, "gh_memcpy_async")
+    # the input gradient on all SMs while the copy engines move the bands
+    st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, gi.data_ptr(),
+                                  ws.data_ptr(), ws.numel(), 0, stream)
+    _lib.check(st, "linear_cross_entropy dH")
+    torch.cuda.current_stream(dev).wait_stream(cs)
+    gw.record_stream(cs)
+    return ce_sum, z_sum, n_valid, gi, gw.T
+
+
 class RowShardedLinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     def forward(ctx, inputs, weight_dv, target, ignore_index, reduction, z_loss_multiplier, fp32_accum, group):
         n_global, scale = _global_scale(target, ignore_index, reduction, group)
         world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if _dp_band_exchange_ok(inputs, weight_dv, world):
+            ce, zs, _, gi, gw = _row_sharded_band_exchange(
+                inputs, weight_dv, target, ignore_index, z_loss_multiplier, fp32_accum, scale, group)
+            loss = (ce + z_loss_multiplier * zs).reshape(1)
+            dist.all_reduce(loss, group=group)
+            loss = (loss * scale).reshape(())
+            ctx.save_for_backward(gi, gw)
+            return loss
         hook = None
         if world > 1:
             def hook(grad_weight: Tensor):

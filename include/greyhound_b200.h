@@ -254,6 +254,9 @@ GH_API int gh_sum_slots(const void* slots, int nslots, int64_t slot_stride, int6
 GH_API int gh_ipc_get_handle(const void* ptr, void* handle_out, size_t* offset_out);
 GH_API int gh_ipc_open(const void* handle, size_t offset, void** ptr_out);
 GH_API int gh_ipc_close(void* ptr, size_t offset);
+/* Device-to-device copy on `stream` (the copy engines; src or dst may be
+ * an IPC mapping of another GPU's memory, then the copy crosses NVLink). */
+GH_API int gh_memcpy_async(void* dst, const void* src, size_t bytes, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Vocab-parallel linear cross-entropy (no counterpart in the reference, which
