@@ -676,7 +676,8 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
     // 1. logits GEMM + fused CE statistics
     {
       const int pair = pick_pair(rows);
-      const int nsub = pick_nsub(rows, V, pair, sms / 2, false, true);
+      // the q store runs on 256-column tiles only
+      const int nsub = q ? 1 : pick_nsub(rows, V, pair, sms / 2, false, true);
       CUtensorMap ta, tb;
       if ((rc = make_operand_maps(&ta, &tb, dtype, Operand{Hc, D, 0}, Operand{W, D, 0}, rows, V, D, pair)))
         return rc;
@@ -696,7 +697,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       p.status = status;
       p.qmode = qmode;
       ProfScope prof(PROF_GEMM_LOGITS_CE, st);
-      if (q) rc = launch_gemm_mm<T, gemm::EPI_LCE_Q, T>(ta, tb, 0, 0, pair, 1, p, sms, st);
+      if (q) rc = launch_gemm_mm<T, gemm::EPI_LCE_Q, T>(ta, tb, 0, 0, pair, nsub, p, sms, st);
       else rc = launch_gemm_mm<T, gemm::EPI_LCE, T>(ta, tb, 0, 0, pair, nsub, p, sms, st);
       if (rc) return rc;
     }

@@ -22,11 +22,8 @@
 // in a fixed order, so results are bit-reproducible run to run.
 #include <mutex>
 
-#include <cstdlib>
-
 #include "common.cuh"
 #include "row_ops.cuh"
-#include "tc_primitives.cuh"
 
 namespace gh {
 namespace {
@@ -71,151 +68,6 @@ ce_fused_kernel(const T* __restrict__ logits, T* dlogits, const int64_t* __restr
         row_grad<T, THREADS, UNROLL, true>(x, y, V, lab, tot.m, coef, scale);
       }
     }
-  }
-}
-
-// CE, streamed shape: each CTA is persistent over rows and moves every row
-// through a ring of shared-memory stages with bulk copies (one thread issues
-// them, completion on mbarriers). A row is read twice: pass 1 (statistics,
-// loads marked L2 evict_last) and pass 2 (gradient, from L2, evict_first).
-// The copy issuer runs kStreamStages chunks ahead across pass and row
-// boundaries, so the next row's first chunks are in flight while this row's
-// gradient is written, and the bytes in flight per SM (2 CTAs x 6 x 16 KB)
-// do not depend on registers. Rows must be 32-byte aligned.
-constexpr int kStreamThreads = 512;
-constexpr int kStreamChunk = kStreamThreads * 32;  // bytes per stage: 32 per thread
-constexpr int kStreamStages = 6;
-constexpr size_t kStreamSmem = (size_t)kStreamStages * kStreamChunk + 1024;
-
-template <typename T>
-__global__ void __launch_bounds__(kStreamThreads, 2)
-ce_stream_kernel(const T* __restrict__ logits, T* dlogits, const int64_t* __restrict__ labels, int64_t rows, int64_t V,
-                 float zmul, int64_t ignore, const float* scale_ptr, float* row_ce, float* row_z, float* lse_out,
-                 int* status) {
-  constexpr int PER = 32 / sizeof(T);               // elements per thread per stage
-  constexpr int64_t CE = kStreamChunk / sizeof(T);  // elements per stage
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint8_t* stage_buf = smem_raw;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)kStreamStages * kStreamChunk);
-  __shared__ float scratch[2 * kStreamThreads / 32];
-  __shared__ int abort_flag;
-  const int tid = threadIdx.x;
-  const int64_t nc = (V + CE - 1) / CE;  // chunks per pass
-  const int passes = dlogits ? 2 : 1;
-  const int64_t my_rows = blockIdx.x < rows ? (rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  const int64_t njobs = my_rows * passes * nc;
-  const int64_t row_bytes = V * (int64_t)sizeof(T);
-  if (tid == 0) {
-    for (int i = 0; i < kStreamStages; ++i) tc::mbar_init(&full[i], 1);
-    abort_flag = 0;
-    tc::fence_barrier_init();
-  }
-  __syncthreads();
-  const uint64_t keep = tc::l2_policy(2), stream = tc::l2_policy(1);
-  // job j: row (j / (passes * nc)), pass ((j / nc) % passes), chunk (j % nc)
-  auto issue = [&](int64_t j) {
-    const int64_t k = j / (passes * nc);
-    const int pass = (int)((j / nc) % passes);
-    const int64_t c = j % nc;
-    const int64_t row = blockIdx.x + k * gridDim.x;
-    const int64_t off = c * kStreamChunk;
-    const uint32_t bytes = (uint32_t)(row_bytes - off < kStreamChunk ? row_bytes - off : kStreamChunk);
-    const int st = (int)(j % kStreamStages);
-    tc::mbar_arrive_expect_tx(&full[st], bytes);
-    tc::bulk_load_hint(stage_buf + (size_t)st * kStreamChunk,
-                       reinterpret_cast<const uint8_t*>(logits + row * V) + off, bytes, &full[st],
-                       (pass == 0 && passes == 2) ? keep : stream);
-  };
-  if (tid == 0)
-    for (int64_t j = 0; j < njobs && j < kStreamStages; ++j) issue(j);
-  int64_t j = 0;
-  bool ok = true;
-  for (int64_t k = 0; k < my_rows && ok; ++k) {
-    const int64_t row = blockIdx.x + k * gridDim.x;
-    const int64_t lab = labels[row];
-    bool valid = lab != ignore;
-    const bool bad = valid && (lab < 0 || lab >= V);
-    valid = valid && !bad;
-    // the label logit is read before this row's (possibly in-place) gradient is written
-    float x_lab = 0.f;
-    if (tid == 0 && valid) x_lab = Elt<T>::to_f(logits[row * V + lab]);
-    MS acc = ms_empty();
-    float lse2 = 0.f, coef = 0.f, sub = 0.f;
-    for (int pass = 0; pass < passes && ok; ++pass) {
-      const bool stats_pass = pass == 0;
-      for (int64_t c = 0; c < nc; ++c, ++j) {
-        const int st = (int)(j % kStreamStages);
-        const uint32_t par = (uint32_t)((j / kStreamStages) & 1);
-        if (!tc::mbar_wait(&full[st], par, &abort_flag, 2000000000ull)) {
-          ok = false;
-          break;
-        }
-        const int64_t col0 = c * CE + (int64_t)tid * PER;
-        if (col0 < V) {
-          const uint4* sp = reinterpret_cast<const uint4*>(stage_buf + (size_t)st * kStreamChunk + tid * 32);
-          const uint4 a = sp[0], b = sp[1];
-          Vec32<T> v;
-          v.raw.w[0] = a.x; v.raw.w[1] = a.y; v.raw.w[2] = a.z; v.raw.w[3] = a.w;
-          v.raw.w[4] = b.x; v.raw.w[5] = b.y; v.raw.w[6] = b.z; v.raw.w[7] = b.w;
-          float f[PER];
-          v.to_float(f);
-          const int nval = V - col0 < PER ? (int)(V - col0) : PER;
-          if (stats_pass) {
-            if (nval == PER) {
-              acc = ms_fold_raw<PER>(acc, f);
-            } else {
-#pragma unroll
-              for (int e = 0; e < PER; ++e)
-                if (e < nval) acc = ms_fold1(acc, f[e] * kLog2e);
-            }
-          } else {
-#pragma unroll
-            for (int e = 0; e < PER; ++e) f[e] = fast_exp2(fmaf(f[e], kLog2e, -lse2)) * coef;
-            const int64_t li = lab - col0;
-            if (valid && li >= 0 && li < PER) {
-#pragma unroll
-              for (int e = 0; e < PER; ++e)
-                if (e == li) f[e] -= sub;
-            }
-            T* y = dlogits + row * V + col0;
-            if (nval == PER) {
-              Vec32<T> o;
-              o.from_float(f);
-              st32_stream(y, o.raw);
-            } else {
-#pragma unroll
-              for (int e = 0; e < PER; ++e)
-                if (e < nval) y[e] = Elt<T>::from_f(f[e]);
-            }
-          }
-        }
-        __syncthreads();  // every thread is done with this stage
-        if (tid == 0 && j + kStreamStages < njobs) issue(j + kStreamStages);
-      }
-      if (stats_pass && ok) {
-        const MS tot = block_merge<kStreamThreads>(acc, scratch);
-        lse2 = tot.m + fast_log2(tot.s);
-        const float lse = lse2 * kLn2;
-        if (tid == 0) {
-          if (bad) atomicOr(status, GH_DEV_BAD_LABEL);
-          row_ce[row] = valid ? lse - x_lab : 0.f;
-          row_z[row] = valid ? lse * lse : 0.f;
-          if (lse_out) lse_out[row] = lse;
-        }
-        const float scale = scale_ptr ? *scale_ptr : 1.f;
-        coef = valid ? scale * (1.f + 2.f * zmul * lse) : 0.f;  // ignored rows: zero gradient
-        sub = valid ? scale : 0.f;
-      }
-    }
-  }
-  if (!ok && tid == 0) {
-    // a stage never completed (not expected for valid addresses): report it
-    // and wait, bounded, for the copies still in flight into this CTA's
-    // shared memory before the CTA leaves
-    atomicOr(status, GH_DEV_PIPELINE_TIMEOUT);
-    volatile int never = 0;
-    for (int64_t jj = j; jj < njobs && jj < j + kStreamStages; ++jj)
-      tc::mbar_wait(&full[jj % kStreamStages], (uint32_t)((jj / kStreamStages) & 1), &never, 2000000000ull);
   }
 }
 
@@ -437,17 +289,6 @@ WsLayout layout(int64_t rows, const Plan& p) {
   return w;
 }
 
-// The streamed CE kernel needs 32-byte aligned rows and buffers (its
-// gradient stores are 32 bytes wide); GREYHOUND_B200_CE_STREAM=0 selects the
-// register-streamed kernel instead.
-template <typename T>
-bool stream_ok(const void* x, const void* y, int64_t V) {
-  const char* e = getenv("GREYHOUND_B200_CE_STREAM");
-  if (e && *e && atoi(e) == 0) return false;
-  return ((V * (int64_t)sizeof(T)) % 32 == 0) &&
-         ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 31) == 0;
-}
-
 template <typename T>
 int launch_ce(const void* logits, void* dlogits, const int64_t* labels, int64_t rows, int64_t V,
               float zmul, int64_t ignore, int mean, const float* gscale, float* ce_sum,
@@ -468,19 +309,7 @@ int launch_ce(const void* logits, void* dlogits, const int64_t* labels, int64_t 
   const float* sp = (mean && y) ? scale : gscale;
   ProfScope prof(PROF_ROWS, st);
   if (rows > 0) {
-    if (p.fused && stream_ok<T>(x, y, V)) {
-      static bool attr_set[64] = {};
-      int dev = 0;
-      cudaGetDevice(&dev);
-      if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaFuncSetAttribute(ce_stream_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kStreamSmem);
-        attr_set[dev] = true;
-      }
-      const int64_t grid = rows < 2 * (int64_t)num_sms() ? rows : 2 * (int64_t)num_sms();
-      ce_stream_kernel<T><<<(unsigned)grid, kStreamThreads, kStreamSmem, st>>>(
-          x, y, labels, rows, V, zmul, ignore, sp, row_ce, row_z, lse_out, status);
-      ++launches;
-    } else if (p.fused) {
+    if (p.fused) {
       int64_t grid = rows;
       const int64_t cap = (int64_t)num_sms() * 2 * 64;
       if (grid > cap) grid = cap;

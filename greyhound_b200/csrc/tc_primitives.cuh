@@ -152,18 +152,6 @@ __device__ __forceinline__ void tma_load_2d_pair_hint(void* smem_dst, const CUte
       : "memory");
 }
 
-// Untiled bulk copy global -> shared of `bytes` (a multiple of 16, both
-// addresses 16-byte aligned), completion on an mbarrier, with an L2 policy.
-// No multicast.
-__device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                               uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
 // ---- tcgen05 ------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* holder_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder_smem)),
