@@ -96,6 +96,9 @@ extern "C" int gh_ipc_get_handle(const void* ptr, void* handle_out, size_t* offs
   if (!ptr || !handle_out || !offset_out) return set_error(GH_EINVAL, "null pointer argument");
   auto range = get_range_fn();
   if (!range) return set_error(GH_ECUDA, "cuMemGetAddressRange unavailable");
+  int dev = 0;  // bind the current device's primary context for the driver call
+  cudaGetDevice(&dev);
+  cudaSetDevice(dev);
   CUdeviceptr base = 0;
   size_t size = 0;
   if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)

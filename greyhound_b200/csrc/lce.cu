@@ -50,6 +50,12 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 // elements, box {64, box_outer}, 128-byte swizzle, zero fill out of bounds.
 int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t inner, int64_t outer, int64_t ld,
              int box_outer) {
+  // A host thread that has made no runtime call yet (autograd's backward
+  // thread for device 0, for one) has no current context, and the driver
+  // call below needs one: bind the current device's primary context.
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaSetDevice(dev);
   auto enc = get_encode();
   if (!enc) return set_error(GH_ECUDA, "cuTensorMapEncodeTiled unavailable");
   const int elt = elt_size(dtype);
