@@ -66,7 +66,7 @@ SIGNATURES: dict[str, tuple] = {
          _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
     "gh_lce_dh_last_chunk": (
-        _i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _i64, _i64, _vp, _vp, _sz, _i32, _vp]
+        _i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _i64, _i64, _vp, _vp, _vp, _sz, _i32, _vp]
     ),
     "gh_gemm": (
         _i32,
@@ -81,7 +81,9 @@ SIGNATURES: dict[str, tuple] = {
         _i32,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
-    "gh_lce_dw_peers": (_i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, ctypes.POINTER(_vp), _i32, _i64, _vp, _sz, _vp]),
+    "gh_lce_dw_peers": (
+        _i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _vp, ctypes.POINTER(_vp), _i32, _i64, _vp, _sz, _vp]
+    ),
     "gh_sum_slots": (_i32, [_vp, _i32, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),
     "gh_ipc_get_handle": (_i32, [_vp, _vp, ctypes.POINTER(_sz)]),
     "gh_ipc_open": (_i32, [_vp, _sz, ctypes.POINTER(_vp)]),
@@ -94,6 +96,7 @@ SIGNATURES: dict[str, tuple] = {
 }
 GH_LCE_DEFER_LAST_DH = 1
 GH_LCE_KEEP_DW_OPERAND = 2
+GH_LCE_GRADS_LATER = 4
 PROF_CLASSES = ("gemm_logits_ce", "gemm_dw", "gemm_dh", "dlogits", "rows", "gemm_other")
 
 _lock = threading.Lock()

@@ -654,12 +654,12 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
   float* row_ce = reinterpret_cast<float*>(ws + L.row_ce);
   float* row_z = reinterpret_cast<float*>(ws + L.row_z);
   float* acc = reinterpret_cast<float*>(ws + L.acc);
-  const bool with_grad = grad_input || grad_weight;
+  const bool with_grad = grad_input || grad_weight || (flags & GH_LCE_GRADS_LATER);
   const bool fp32_accum = L.need_acc;
   // q mode is decided by the layout alone (dtype and GREYHOUND_B200_LCE_Q),
   // so the calls that continue this one from the workspace agree with it
   const bool q = L.q && with_grad;
-  const bool q_dw = q && (grad_weight || (flags & GH_LCE_KEEP_DW_OPERAND));
+  const bool q_dw = q && (grad_weight || (flags & (GH_LCE_KEEP_DW_OPERAND | GH_LCE_GRADS_LATER)));
   uint8_t* qmode = reinterpret_cast<uint8_t*>(ws + L.qmode);
   float* alpha = reinterpret_cast<float*>(ws + L.alpha);
   int* rowflag = reinterpret_cast<int*>(ws + L.rowflag);
@@ -865,8 +865,13 @@ extern "C" int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* targe
   if (D % 8) return set_error(GH_EUNSUPPORTED, "hidden size must be a multiple of 8 (got %lld)", (long long)D);
   if (!H || !W || !target || !ce_sum || !z_sum || !n_valid || !workspace)
     return set_error(GH_EINVAL, "null pointer argument");
-  const bool loss_only = !grad_input && !grad_weight;
+  const bool later = flags & GH_LCE_GRADS_LATER;
+  const bool loss_only = !grad_input && !grad_weight && !later;
+  if (later && (grad_input || grad_weight))
+    return set_error(GH_EINVAL, "GH_LCE_GRADS_LATER takes no gradient buffers");
   LceLayout L = lce_layout(N, D, V, chunk_rows, dtype, fp32_grad_weight_accum, loss_only);
+  if (later && N > L.chunk)
+    return set_error(GH_EUNSUPPORTED, "GH_LCE_GRADS_LATER needs all rows in one chunk");
   if (workspace_bytes < L.total)
     return set_error(GH_EWORKSPACE, "workspace too small: %zu < %zu", workspace_bytes, L.total);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -885,8 +890,8 @@ extern "C" int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* targe
 
 extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype, int64_t chunk_rows,
                                     int fp32_grad_weight_accum, int64_t row_begin, int64_t row_end,
-                                    void* grad_input, void* workspace, size_t workspace_bytes, int max_ctas,
-                                    void* stream) {
+                                    const float* scale, void* grad_input, void* workspace, size_t workspace_bytes,
+                                    int max_ctas, void* stream) {
   if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
   if (N <= 0) return GH_OK;
   if (!W || !grad_input || !workspace) return set_error(GH_EINVAL, "null pointer argument");
@@ -910,15 +915,15 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
   int* status = reinterpret_cast<int*>(ws + L.status);
   const int rc = run_gemm(dtype, A, B, row_end - row_begin, D, V,
                           static_cast<char*>(grad_input) + (s0 + row_begin) * D * elt, dtype, D, nullptr, nullptr, 0,
-                          nullptr, 1, max_ctas, static_cast<cudaStream_t>(stream), status, PROF_GEMM_DH, Hints{},
+                          scale, 1, max_ctas, static_cast<cudaStream_t>(stream), status, PROF_GEMM_DH, Hints{},
                           ws + L.dh2 + (size_t)row_begin * D * elt,
                           q ? reinterpret_cast<const float*>(ws + L.alpha) + row_begin : nullptr);
   return rc ? rc : publish_status(status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, int dtype, int64_t chunk_rows,
-                               int fp32_grad_weight_accum, void* const* band_out, int nbands, int64_t band_rows,
-                               void* workspace, size_t workspace_bytes, void* stream) {
+                               int fp32_grad_weight_accum, const float* scale, void* const* band_out, int nbands,
+                               int64_t band_rows, void* workspace, size_t workspace_bytes, void* stream) {
   if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
   if (N < 0 || D <= 0 || V <= 0) return set_error(GH_EINVAL, "bad shape");
   if (!H || !band_out || !workspace) return set_error(GH_EINVAL, "null pointer argument");
@@ -936,11 +941,12 @@ extern "C" int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, i
   po.n = nbands;
   po.rows = band_rows;
   for (int i = 0; i < nbands; ++i) po.ptr[i] = band_out[i];
-  // q mode: gh_lce_fwd_bwd(..., GH_LCE_KEEP_DW_OPERAND) left alpha * H in the workspace
+  // q mode: gh_lce_fwd_bwd(..., GH_LCE_KEEP_DW_OPERAND or GH_LCE_GRADS_LATER)
+  // left alpha * H in the workspace
   Operand A{ws + L.logits, L.ldl, 1};
   Operand B = L.q ? Operand{ws + L.hs, D, 1} : Operand{H, D, 1};
   int* status = reinterpret_cast<int*>(ws + L.status);
-  const int rc = run_gemm(dtype, A, B, V, D, N, nullptr, dtype, D, nullptr, nullptr, 0, nullptr, 1, num_sms_dev(), st,
+  const int rc = run_gemm(dtype, A, B, V, D, N, nullptr, dtype, D, nullptr, nullptr, 0, scale, 1, num_sms_dev(), st,
                           status, PROF_GEMM_DW, kStreamA_KeepB, nullptr, nullptr, &po);
   return rc ? rc : publish_status(status, st);
 }

@@ -151,13 +151,15 @@ def _dp_band_exchange_ok(inputs, weight_dv, world) -> bool:
             and lce.chunk_size_for(B, D, V, inputs.element_size()) >= B)
 
 
-def _row_sharded_band_exchange(inputs, weight_dv, target, ignore_index, z_loss_multiplier, fp32_accum, scale,
-                               group):
-    """Data-parallel step whose weight-gradient all-reduce is a reduce-scatter
-    fused into the dW GEMM's epilogue (each tile stored in the owner rank's
-    receive slot), a fixed-order sum of the slots on each owner, and copies
-    of the reduced bands between the ranks by the copy engines, overlapped
-    with the input-gradient GEMM on all SMs."""
+def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
+    """Backward of the data-parallel step (the forward kept the gradient
+    operands in ``ws``, ``lce.linear_cross_entropy_stats_keep``). The weight
+    gradient's all-reduce is a reduce-scatter fused into the dW GEMM's
+    epilogue (each tile stored in the owner rank's receive slot), a
+    fixed-order sum of the slots on each owner, and copies of the reduced
+    bands between the ranks by the copy engines, overlapped with the
+    input-gradient GEMM on all SMs. Both gradients come out multiplied by
+    ``grad_output``."""
     from greyhound_b200 import _lib
 
     B, D = inputs.shape
@@ -165,30 +167,18 @@ def _row_sharded_band_exchange(inputs, weight_dv, target, ignore_index, z_loss_m
     dev = inputs.device
     ex = _BandExchange.get(group, dev, V, D, inputs.dtype)
     lib = ex.lib
-    _lib.raise_pending(dev, "row_sharded_linear_cross_entropy")
+    _lib.raise_pending(dev, "row_sharded_linear_cross_entropy backward")
     x = inputs.contiguous()
     w = lce._weight_vd(weight_dv)
-    t = target.contiguous()
     code = _lib.dtype_code(inputs.dtype)
     chunk = lce.chunk_size_for(B, D, V, inputs.element_size())
-    ws = _lib.workspace(lib.gh_lce_workspace_bytes(B, D, V, chunk, code, int(fp32_accum)), dev)
-    ce_sum = torch.empty((), dtype=torch.float32, device=dev)
-    z_sum = torch.empty((), dtype=torch.float32, device=dev)
-    n_valid = torch.empty((), dtype=torch.float32, device=dev)
     gi = torch.empty((B, D), dtype=inputs.dtype, device=dev)
     gw = torch.empty((V, D), dtype=inputs.dtype, device=dev)
-    gs = scale.reshape(1).float().contiguous()
+    g = grad_output.reshape(1).float().contiguous()
     stream = _lib.stream_of(x)
-    # logits GEMM + statistics + the gradient operands; no dW, dH deferred
-    st = lib.gh_lce_fwd_bwd(
-        x.data_ptr(), w.data_ptr(), t.data_ptr(), B, D, V, code, float(z_loss_multiplier), int(ignore_index), 0,
-        gs.data_ptr(), chunk, int(fp32_accum), _lib.GH_LCE_DEFER_LAST_DH | _lib.GH_LCE_KEEP_DW_OPERAND,
-        gi.data_ptr(), None, ce_sum.data_ptr(), z_sum.data_ptr(), n_valid.data_ptr(), ws.data_ptr(), ws.numel(),
-        stream)
-    _lib.check(st, "linear_cross_entropy")
     # dW, each band's tiles stored straight into its owner's receive slot
-    st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), ex.band_out, ex.world,
-                             ex.band_rows, ws.data_ptr(), ws.numel(), stream)
+    st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), g.data_ptr(), ex.band_out,
+                             ex.world, ex.band_rows, ws.data_ptr(), ws.numel(), stream)
     _lib.check(st, "gh_lce_dw_peers")
     ex.barrier()  # every rank's slot of my band has arrived
     me = ex.rank
@@ -207,12 +197,12 @@ def _row_sharded_band_exchange(inputs, weight_dv, target, ignore_index, z_loss_m
                                      cs.cuda_stream)
             _lib.check(st, "gh_memcpy_async")
     # the input gradient on all SMs while the copy engines move the bands
-    st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, gi.data_ptr(),
-                                  ws.data_ptr(), ws.numel(), 0, stream)
+    st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, g.data_ptr(),
+                                  gi.data_ptr(), ws.data_ptr(), ws.numel(), 0, stream)
     _lib.check(st, "linear_cross_entropy dH")
     torch.cuda.current_stream(dev).wait_stream(cs)
     gw.record_stream(cs)
-    return ce_sum, z_sum, n_valid, gi, gw.T
+    return gi, gw.T
 
 
 class RowShardedLinearCrossEntropy(torch.autograd.Function):
@@ -221,13 +211,16 @@ class RowShardedLinearCrossEntropy(torch.autograd.Function):
         n_global, scale = _global_scale(target, ignore_index, reduction, group)
         world = dist.get_world_size(group) if dist.is_initialized() else 1
         if _dp_band_exchange_ok(inputs, weight_dv, world):
-            ce, zs, _, gi, gw = _row_sharded_band_exchange(
-                inputs, weight_dv, target, ignore_index, z_loss_multiplier, fp32_accum, scale, group)
+            # loss now; both gradients and the weight-gradient exchange in the backward
+            ce, zs, _, ws = lce.linear_cross_entropy_stats_keep(
+                inputs, weight_dv, target, z_loss_multiplier, fp32_accum, ignore_index, False, grad_scale=scale)
             loss = (ce + z_loss_multiplier * zs).reshape(1)
             dist.all_reduce(loss, group=group)
             loss = (loss * scale).reshape(())
-            ctx.save_for_backward(gi, gw)
+            ctx.band = (fp32_accum, group)
+            ctx.save_for_backward(ws, inputs, weight_dv)
             return loss
+        ctx.band = None
         hook = None
         if world > 1:
             def hook(grad_weight: Tensor):
@@ -245,6 +238,10 @@ class RowShardedLinearCrossEntropy(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, g):
+        if ctx.band is not None:
+            ws, inputs, weight_dv = ctx.saved_tensors
+            gi, gw = _band_exchange_grads(ws, inputs, weight_dv, g, *ctx.band)
+            return gi, gw, None, None, None, None, None, None
         gi, gw = ctx.saved_tensors
         return scale_by(gi, g), scale_by(gw, g), None, None, None, None, None, None
 

@@ -130,14 +130,14 @@ def _tc_lce(inputs, weight, target, z, fp32_accum, ignore_index, mean, grad_scal
         else:
             split, ctas = last_rows, 0  # whole dH on all SMs, overlapping the collective
         st = lib.gh_lce_dh_last_chunk(
-            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, split, gi.data_ptr(), ws.data_ptr(),
+            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, split, None, gi.data_ptr(), ws.data_ptr(),
             ws.numel(), ctas, stream,
         )
         _lib.check(st, "linear_cross_entropy dH")
         if work is not None:
             work.wait()
         st = lib.gh_lce_dh_last_chunk(
-            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), split, -1, gi.data_ptr(), ws.data_ptr(),
+            w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), split, -1, None, gi.data_ptr(), ws.data_ptr(),
             ws.numel(), 0, stream,
         )
         _lib.check(st, "linear_cross_entropy dH")
@@ -209,6 +209,97 @@ def linear_cross_entropy_with_grad(
             work.wait()
     grad_weight = grad_weight_vd.T
     return ce_sum, z_sum, n_valid, grad_input, grad_weight
+
+
+def two_phase_ok(inputs: Tensor, weight: Tensor) -> bool:
+    """Whether the loss / gradient split applies (gradients computed in the
+    backward, already scaled by grad_output): tcgen05 operands and all rows
+    in one chunk (the Llama-3-8B head's case). GREYHOUND_B200_LCE_TWO_PHASE=0
+    keeps the reference's gradients-in-forward schedule."""
+    if os.environ.get("GREYHOUND_B200_LCE_TWO_PHASE", "1") in ("0", ""):
+        return False
+    if inputs.ndim != 2 or weight.ndim != 2 or not inputs.is_cuda or not _tc_ok(inputs, weight):
+        return False
+    B, D = inputs.shape
+    V = weight.shape[1]
+    return B > 0 and chunk_size_for(B, D, V, inputs.element_size()) >= B
+
+
+def lce_workspace_bytes(inputs: Tensor, weight: Tensor, fp32_accum: bool) -> int:
+    from greyhound_b200 import _lib
+
+    B, D = inputs.shape
+    V = weight.shape[1]
+    chunk = chunk_size_for(B, D, V, inputs.element_size())
+    return max(int(_lib.load().gh_lce_workspace_bytes(B, D, V, chunk, _lib.dtype_code(inputs.dtype),
+                                                       int(fp32_accum))), 256)
+
+
+def linear_cross_entropy_stats_keep(inputs: Tensor, weight: Tensor, target: Tensor, z_loss_multiplier: float,
+                                    fp32_accum: bool, ignore_index: int, mean_reduction: bool,
+                                    grad_scale: Tensor | None = None) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """Phase 1 of the split: ``(ce_sum, z_sum, n_valid, workspace)``. The
+    workspace keeps what both gradient GEMMs need (the stored e^x tile and
+    the per-row factors, with the mean / grad_scale folded in) for
+    ``linear_cross_entropy_grads_from``."""
+    from greyhound_b200 import _lib
+
+    _check(inputs, weight, target)
+    B, D = inputs.shape
+    V = weight.shape[1]
+    x = inputs.contiguous()
+    w = _weight_vd(weight)
+    t = target.contiguous()
+    dev = inputs.device
+    lib = _lib.load()
+    _lib.raise_pending(dev, "linear_cross_entropy")
+    chunk = chunk_size_for(B, D, V, inputs.element_size())
+    ws = _lib.workspace(lce_workspace_bytes(inputs, weight, fp32_accum), dev)
+    ce_sum = torch.empty((), dtype=torch.float32, device=dev)
+    z_sum = torch.empty((), dtype=torch.float32, device=dev)
+    n_valid = torch.empty((), dtype=torch.float32, device=dev)
+    gs = grad_scale.reshape(1).float().contiguous() if grad_scale is not None else None
+    st = lib.gh_lce_fwd_bwd(
+        x.data_ptr(), w.data_ptr(), t.data_ptr(), B, D, V, _lib.dtype_code(inputs.dtype), float(z_loss_multiplier),
+        int(ignore_index), int(mean_reduction), _lib.ptr(gs), chunk, int(fp32_accum), _lib.GH_LCE_GRADS_LATER,
+        None, None, ce_sum.data_ptr(), z_sum.data_ptr(), n_valid.data_ptr(), ws.data_ptr(), ws.numel(),
+        _lib.stream_of(x))
+    _lib.check(st, "linear_cross_entropy")
+    _lib.raise_on_status(ws, "linear_cross_entropy")
+    return ce_sum, z_sum, n_valid, ws
+
+
+def linear_cross_entropy_grads_from(ws: Tensor, inputs: Tensor, weight: Tensor, fp32_accum: bool,
+                                    grad_output: Tensor | None) -> tuple[Tensor, Tensor]:
+    """Phase 2: ``(grad_input [B, D], grad_weight [D, V] view)`` times
+    ``grad_output`` from the workspace of ``linear_cross_entropy_stats_keep``
+    (the dW GEMM, then the dH GEMM)."""
+    import ctypes
+
+    from greyhound_b200 import _lib
+
+    B, D = inputs.shape
+    V = weight.shape[1]
+    x = inputs.contiguous()
+    w = _weight_vd(weight)
+    dev = inputs.device
+    lib = _lib.load()
+    _lib.raise_pending(dev, "linear_cross_entropy backward")
+    code = _lib.dtype_code(inputs.dtype)
+    chunk = chunk_size_for(B, D, V, inputs.element_size())
+    g = grad_output.reshape(1).float().contiguous() if grad_output is not None else None
+    stream = _lib.stream_of(x)
+    gw = torch.empty((V, D), dtype=weight.dtype, device=dev)
+    band = (ctypes.c_void_p * 1)(gw.data_ptr())  # one band: this GPU's own gradient
+    st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), _lib.ptr(g), band, 1,
+                             -(-V // 256) * 256, ws.data_ptr(), ws.numel(), stream)
+    _lib.check(st, "linear_cross_entropy dW")
+    gi = torch.empty((B, D), dtype=inputs.dtype, device=dev)
+    st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, _lib.ptr(g),
+                                  gi.data_ptr(), ws.data_ptr(), ws.numel(), 0, stream)
+    _lib.check(st, "linear_cross_entropy dH")
+    _lib.raise_on_status(ws, "linear_cross_entropy backward")
+    return gi, gw.T
 
 
 def linear_cross_entropy_loss(

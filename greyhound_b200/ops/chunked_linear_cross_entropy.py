@@ -29,8 +29,12 @@ from torch import Tensor
 
 from greyhound_b200.ops.scale import scale_by
 from greyhound_b200.kernels.linear_cross_entropy import (
+    lce_workspace_bytes,
+    linear_cross_entropy_grads_from,
     linear_cross_entropy_loss,
+    linear_cross_entropy_stats_keep,
     linear_cross_entropy_with_grad,
+    two_phase_ok,
 )
 
 __all__ = [
@@ -38,6 +42,8 @@ __all__ = [
     "chunked_linear_cross_entropy_fwd",
     "chunked_linear_cross_entropy_fwd_mean",
     "chunked_linear_cross_entropy_loss",
+    "chunked_linear_cross_entropy_stats",
+    "chunked_linear_cross_entropy_grads",
 ]
 
 
@@ -137,6 +143,50 @@ def _(
     return _fake(inputs, weight)[:3]
 
 
+@torch.library.custom_op("greyhound::chunked_linear_cross_entropy_stats", mutates_args=())
+def chunked_linear_cross_entropy_stats(
+    inputs: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    z_loss_multiplier: float,
+    fp32_grad_weight_accum: bool,
+    ignore_index: int,
+    mean_reduction: bool,
+) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """(ce_sum, z_sum, n_valid, workspace): the loss of the single-chunk
+    training path with everything the two gradient GEMMs need kept in the
+    workspace (uint8) for ``chunked_linear_cross_entropy_grads``."""
+    return linear_cross_entropy_stats_keep(inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum,
+                                           ignore_index, mean_reduction)
+
+
+@chunked_linear_cross_entropy_stats.register_fake
+def _(inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index, mean_reduction):
+    f = _fake(inputs, weight)
+    ws = torch.empty(lce_workspace_bytes(inputs, weight, fp32_grad_weight_accum), dtype=torch.uint8,
+                     device=inputs.device)
+    return f[0], f[1], f[2], ws
+
+
+@torch.library.custom_op("greyhound::chunked_linear_cross_entropy_grads", mutates_args=())
+def chunked_linear_cross_entropy_grads(
+    workspace: Tensor,
+    inputs: Tensor,
+    weight: Tensor,
+    grad_output: Tensor,
+    fp32_grad_weight_accum: bool,
+) -> tuple[Tensor, Tensor]:
+    """(grad_input [B, D], grad_weight [D, V]) times grad_output, from the
+    workspace of ``chunked_linear_cross_entropy_stats``."""
+    return linear_cross_entropy_grads_from(workspace, inputs, weight, fp32_grad_weight_accum, grad_output)
+
+
+@chunked_linear_cross_entropy_grads.register_fake
+def _(workspace, inputs, weight, grad_output, fp32_grad_weight_accum):
+    f = _fake(inputs, weight)
+    return f[3], f[4]
+
+
 def _forward_only_chunked_ce(
     inputs: Tensor,
     weight: Tensor,
@@ -173,6 +223,24 @@ class ChunkedLinearCrossEntropyFunction(torch.autograd.Function):
             return _forward_only_chunked_ce(
                 inputs, weight, target, ignore_index, reduction, z_loss_multiplier
             )
+        if reduction not in ("mean", "sum"):
+            raise ValueError(f"Unsupported reduction: {reduction}")
+        if two_phase_ok(inputs, weight):
+            # loss now, gradients in the backward already multiplied by
+            # grad_output: no scaling pass, and a second backward through a
+            # retained graph recomputes them with its own grad_output
+            ce_sum, z_sum, n_valid, ws = chunked_linear_cross_entropy_stats(
+                inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index,
+                reduction == "mean"
+            )
+            loss = ce_sum + z_loss_multiplier * z_sum
+            if reduction == "mean":
+                loss = loss / n_valid.clamp(min=1.0)
+            ctx.two_phase = True  # type: ignore[attr-defined]
+            ctx.fp32_accum = fp32_grad_weight_accum  # type: ignore[attr-defined]
+            ctx.save_for_backward(ws, inputs, weight)  # type: ignore[attr-defined]
+            return loss
+        ctx.two_phase = False  # type: ignore[attr-defined]
         if reduction == "mean":
             ce_sum, z_sum, n_valid, grad_input, grad_weight = chunked_linear_cross_entropy_fwd_mean(
                 inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index
@@ -190,6 +258,11 @@ class ChunkedLinearCrossEntropyFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx: object, grad_output: Tensor):  # type: ignore[override]
+        if ctx.two_phase:  # type: ignore[attr-defined]
+            ws, inputs, weight = ctx.saved_tensors  # type: ignore[attr-defined]
+            gi, gw = chunked_linear_cross_entropy_grads(ws, inputs, weight, grad_output,
+                                                        ctx.fp32_accum)  # type: ignore[attr-defined]
+            return gi, gw, None, None, None, None, None
         grad_input, grad_weight, _ = ctx.saved_tensors  # type: ignore[attr-defined]
         return (
             scale_by(grad_input, grad_output),

@@ -193,10 +193,15 @@ GH_API int gh_logits_grad(const void* logits, void* dlogits, const int64_t* labe
  *          computed; call gh_lce_dh_last_chunk later (lets a data-parallel
  *          caller start the grad_weight all-reduce first);
  *          GH_LCE_KEEP_DW_OPERAND with grad_weight == NULL -> leave the weight
- *          gradient's operands in the workspace for gh_lce_dw_peers
+ *          gradient's operands in the workspace for gh_lce_dw_peers;
+ *          GH_LCE_GRADS_LATER with both gradient pointers NULL and all rows
+ *          in one chunk -> loss plus everything both gradient GEMMs need, kept
+ *          in the workspace; the gradients come later from gh_lce_dw_peers
+ *          and gh_lce_dh_last_chunk, scaled by the autograd grad_output (so
+ *          the backward needs no separate scaling pass)
  *   ce_sum, z_sum, n_valid: float scalars (overwritten)
  * ------------------------------------------------------------------------ */
-enum { GH_LCE_DEFER_LAST_DH = 1, GH_LCE_KEEP_DW_OPERAND = 2 };
+enum { GH_LCE_DEFER_LAST_DH = 1, GH_LCE_KEEP_DW_OPERAND = 2, GH_LCE_GRADS_LATER = 4 };
 
 GH_API size_t gh_lce_workspace_bytes(int64_t N, int64_t D, int64_t V, int64_t chunk_rows,
                                      int dtype, int fp32_grad_weight_accum);
@@ -215,16 +220,18 @@ GH_API int gh_lce_fwd_bwd(const void* H, const void* W, const int64_t* target,
                           void* workspace, size_t workspace_bytes, void* stream);
 /* grad_input rows [row_begin, row_end) of the last chunk (offsets inside the
  * chunk; row_end < 0: to the end), from what gh_lce_fwd_bwd(...,
- * GH_LCE_DEFER_LAST_DH) left in the workspace. max_ctas <= 0: all SMs;
- * fewer leave SMs to a concurrently running collective. */
+ * GH_LCE_DEFER_LAST_DH or GH_LCE_GRADS_LATER) left in the workspace, times
+ * *scale when scale != NULL (a device float). max_ctas <= 0: all SMs; fewer
+ * leave SMs to a concurrently running collective. */
 GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, int dtype,
                                 int64_t chunk_rows, int fp32_grad_weight_accum,
-                                int64_t row_begin, int64_t row_end,
+                                int64_t row_begin, int64_t row_end, const float* scale,
                                 void* grad_input, void* workspace, size_t workspace_bytes,
                                 int max_ctas, void* stream);
 
-/* Weight gradient of a single-chunk call (N <= chunk rows) whose
- * gh_lce_fwd_bwd ran with grad_weight == NULL and GH_LCE_KEEP_DW_OPERAND,
+/* Weight gradient (times *scale when scale != NULL, a device float) of a
+ * single-chunk call (N <= chunk rows) whose gh_lce_fwd_bwd ran with
+ * grad_weight == NULL and GH_LCE_KEEP_DW_OPERAND or GH_LCE_GRADS_LATER,
  * stored in row bands: rows [b * band_rows, (b + 1) * band_rows) of the
  * [V, D] gradient go to band_out[b] (row-major, pitch D), b < nbands <= 8,
  * band_rows a multiple of 256. band_out[b] may point into another GPU's
@@ -234,7 +241,7 @@ GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, 
  * which is single-device). The kernel ends with a system-scope fence, so
  * once it has completed the stores are visible to the owners. */
 GH_API int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, int dtype,
-                           int64_t chunk_rows, int fp32_grad_weight_accum,
+                           int64_t chunk_rows, int fp32_grad_weight_accum, const float* scale,
                            void* const* band_out, int nbands, int64_t band_rows,
                            void* workspace, size_t workspace_bytes, void* stream);
 
