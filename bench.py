@@ -86,8 +86,13 @@ def max_over_ranks(x: float, world: int) -> float:
     import torch.distributed as dist
 
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    allv = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(allv, t)
+    PER_RANK.append([round(float(v.item()), 4) for v in allv])
+    return max(float(v.item()) for v in allv)
+
+
+PER_RANK: list = []  # every max_over_ranks call's per-rank values, for the JSON line
 
 
 # --------------------------------------------------------------------------- clocks
@@ -361,6 +366,8 @@ def bench_lce(args, rank, world, local):
         "clocks": clocks,
         "peak_mem_mb": peak_mem_mb,
     }
+    if world > 1:
+        line["ms_per_rank"] = {"device": PER_RANK[0], "e2e": PER_RANK[-1]}
     del H, W, bufs
     torch.cuda.empty_cache()
     if rows_block is not None:

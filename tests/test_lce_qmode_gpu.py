@@ -142,3 +142,28 @@ def test_q_store_matches_the_dlogits_pipeline(monkeypatch):
     assert abs(q[0] - ref[0]) <= 1e-5 * abs(ref[0])
     assert _maxabs_norm(q[1], ref[1]) <= 1e-2
     assert _maxabs_norm(q[2], ref[2]) <= 1e-2
+
+
+@requires_gpu
+def test_gradients_in_backward_follow_grad_output(monkeypatch):
+    """Single-chunk calls compute both gradients in the backward, multiplied
+    by grad_output in the GEMM epilogues: a retained graph's second backward
+    with another grad_output gives that multiple, and the results match the
+    gradients-in-forward schedule (GREYHOUND_B200_LCE_TWO_PHASE=0)."""
+    H, W, t = _inputs(512, 256, 8000, 48, 0.05, ign=0.05)
+    dev = torch.device("cuda", 0)
+    Hd = torch.from_numpy(H).to(dev, torch.bfloat16).requires_grad_(True)
+    Wd = torch.from_numpy(W).to(dev, torch.bfloat16).requires_grad_(True)
+    loss = chunked_linear_cross_entropy(Hd, Wd, torch.from_numpy(t).to(dev), z_loss_multiplier=1e-4)
+    loss.backward(retain_graph=True)
+    g1 = (Hd.grad.float().clone(), Wd.grad.float().clone())
+    Hd.grad = None
+    Wd.grad = None
+    loss.backward(torch.tensor(2.5, device=dev))
+    for a, b in zip((Hd.grad.float(), Wd.grad.float()), g1):
+        assert (a - 2.5 * b).abs().max() <= 1e-2 * (2.5 * b).abs().max()
+    monkeypatch.setenv("GREYHOUND_B200_LCE_TWO_PHASE", "0")
+    ref = _run(H, W, t, "mean", 1e-4)
+    assert abs(loss.item() - ref[0]) <= 1e-5 * abs(ref[0])
+    assert _maxabs_norm(g1[0].cpu().numpy(), ref[1]) <= 1e-2
+    assert _maxabs_norm(g1[1].cpu().numpy(), ref[2]) <= 1e-2
