@@ -368,6 +368,10 @@ def bench_lce(args, rank, world, local):
     }
     if world > 1:
         line["ms_per_rank"] = {"device": PER_RANK[0], "e2e": PER_RANK[-1]}
+        from greyhound_b200 import distributed as _dd
+
+        if _dd._DP_TIMING:
+            line["dp_phases_ms"] = _dd.dp_phase_summary()
     del H, W, bufs
     torch.cuda.empty_cache()
     if rows_block is not None:

@@ -151,6 +151,28 @@ def _dp_band_exchange_ok(inputs, weight_dv, world) -> bool:
             and lce.chunk_size_for(B, D, V, inputs.element_size()) >= B)
 
 
+_DP_TIMING = __import__("os").environ.get("GREYHOUND_B200_DP_TIMING", "0") not in ("", "0")
+DP_PHASES: list = []  # per backward: [(phase, CUDA event)], when _DP_TIMING
+
+
+def dp_phase_summary() -> dict:
+    """Mean ms of each band-exchange phase (from the previous mark) over the
+    recorded backwards; synchronises. Copies are measured from barrier2."""
+    torch.cuda.synchronize()
+    acc: dict = {}
+    for marks in DP_PHASES:
+        d = dict(marks)
+        prev = None
+        for name, ev in marks:
+            if prev is not None:
+                ref = d["barrier2"] if name == "copies_done" else prev
+                acc.setdefault(name, []).append(ref.elapsed_time(ev))
+            if name != "copies_done":
+                prev = ev
+    DP_PHASES.clear()
+    return {k: sum(v) / len(v) for k, v in acc.items()}
+
+
 def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
     """Backward of the data-parallel step (the forward kept the gradient
     operands in ``ws``, ``lce.linear_cross_entropy_stats_keep``). The weight
@@ -176,16 +198,29 @@ def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
     gw = torch.empty((V, D), dtype=inputs.dtype, device=dev)
     g = grad_output.reshape(1).float().contiguous()
     stream = _lib.stream_of(x)
+    marks = []
+
+    def mark(name, st_=None):  # phase timing with CUDA events (GREYHOUND_B200_DP_TIMING=1)
+        if _DP_TIMING:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(st_)
+            marks.append((name, ev))
+
+    mark("start")
     # dW, each band's tiles stored straight into its owner's receive slot
     st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), g.data_ptr(), ex.band_out,
                              ex.world, ex.band_rows, ws.data_ptr(), ws.numel(), stream)
     _lib.check(st, "gh_lce_dw_peers")
+    mark("dw_gemm")
     ex.barrier()  # every rank's slot of my band has arrived
+    mark("barrier1")
     me = ex.rank
     st = lib.gh_sum_slots(ex.recv.data_ptr(), ex.world, ex.band_rows * D, ex.rows_of(me), D, D, code,
                           ex.shard.data_ptr(), gw[me * ex.band_rows:].data_ptr(), stream)
     _lib.check(st, "gh_sum_slots")
+    mark("sum_slots")
     ex.barrier()  # every rank's reduced band is ready
+    mark("barrier2")
     ready = torch.cuda.Event()
     ready.record()
     cs = ex.copy_stream
@@ -196,12 +231,17 @@ def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
             st = lib.gh_memcpy_async(gw[r * ex.band_rows:].data_ptr(), ex.shard_src[r], ex.rows_of(r) * D * elt,
                                      cs.cuda_stream)
             _lib.check(st, "gh_memcpy_async")
+    mark("copies_done", cs)
     # the input gradient on all SMs while the copy engines move the bands
     st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, g.data_ptr(),
                                   gi.data_ptr(), ws.data_ptr(), ws.numel(), 0, stream)
     _lib.check(st, "linear_cross_entropy dH")
+    mark("dh_gemm")
     torch.cuda.current_stream(dev).wait_stream(cs)
+    mark("joined")
     gw.record_stream(cs)
+    if _DP_TIMING:
+        DP_PHASES.append(marks)
     return gi, gw.T
 
 
