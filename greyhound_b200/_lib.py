@@ -82,7 +82,7 @@ SIGNATURES: dict[str, tuple] = {
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i32, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp],
     ),
     "gh_lce_dw_peers": (
-        _i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _vp, ctypes.POINTER(_vp), _i32, _i64, _vp, _sz, _vp]
+        _i32, [_vp, _i64, _i64, _i64, _i32, _i64, _i32, _vp, ctypes.POINTER(_vp), _i32, _i64, _i32, _vp, _sz, _vp]
     ),
     "gh_sum_slots": (_i32, [_vp, _i32, _i64, _i64, _i64, _i64, _i32, _vp, _vp, _vp]),
     "gh_ipc_get_handle": (_i32, [_vp, _vp, ctypes.POINTER(_sz)]),

@@ -317,6 +317,7 @@ int add_partial(void* out, const void* part, int64_t rows, int64_t cols, int64_t
 struct PeerOut {
   int n = 0;
   int64_t rows = 0;
+  int first = 0;  // band whose tiles this GEMM computes first
   void* ptr[gemm::kMaxPeers] = {};
 };
 
@@ -361,6 +362,8 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
       return set_error(GH_EUNSUPPORTED, "peer output: 16-bit output, no split-K, <= %d bands of a multiple of %d rows",
                        gemm::kMaxPeers, 2 * BM);
     p.npeer = peers->n;
+    // start on band `first` (raster 1 walks the output rows band by band)
+    if (raster == 1) p.tile_rot = (int)(((int64_t)peers->first * (peers->rows / (BM * pair)) * p.num_n) % p.num_tiles);
     p.peer_rows = peers->rows;
     for (int i = 0; i < peers->n; ++i) {
       p.peer_out[i] = peers->ptr[i];
@@ -923,7 +926,8 @@ extern "C" int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t
 
 extern "C" int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, int dtype, int64_t chunk_rows,
                                int fp32_grad_weight_accum, const float* scale, void* const* band_out, int nbands,
-                               int64_t band_rows, void* workspace, size_t workspace_bytes, void* stream) {
+                               int64_t band_rows, int first_band, void* workspace, size_t workspace_bytes,
+                               void* stream) {
   if (dtype != GH_BF16 && dtype != GH_F16) return set_error(GH_ETYPE, "bf16 or fp16 expected");
   if (N < 0 || D <= 0 || V <= 0) return set_error(GH_EINVAL, "bad shape");
   if (!H || !band_out || !workspace) return set_error(GH_EINVAL, "null pointer argument");
@@ -940,6 +944,7 @@ extern "C" int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, i
   PeerOut po;
   po.n = nbands;
   po.rows = band_rows;
+  po.first = first_band >= 0 && first_band < nbands ? first_band : 0;
   for (int i = 0; i < nbands; ++i) po.ptr[i] = band_out[i];
   // q mode: gh_lce_fwd_bwd(..., GH_LCE_KEEP_DW_OPERAND or GH_LCE_GRADS_LATER)
   // left alpha * H in the workspace

@@ -96,6 +96,9 @@ struct Params {
   // which may be another GPU's memory: the GEMM's tiles go straight to the
   // rank that reduces that band (a reduce-scatter fused into the epilogue).
   int npeer;
+  // tile order rotated by this many tiles (band-store GEMMs start on their
+  // own rank's band, so the ranks do not all write to one owner at a time)
+  int tile_rot;
   int64_t peer_rows;
   void* peer_out[kMaxPeers];
   // L2 policy of each operand's TMA loads (0 none, 1 evict_first, 2 evict_last)
@@ -154,6 +157,7 @@ __device__ __forceinline__ TileK tile_k(const Params& p, int tile, int nkb) {
   TileK t;
   const int nsplit = p.ksplit > 1 ? p.ksplit : 1;
   const int per_slice = p.num_m * p.num_n;
+  if (p.tile_rot) tile = (tile + p.tile_rot) % p.num_tiles;
   t.ks = nsplit > 1 ? tile / per_slice : 0;
   tile_coords(p, tile - t.ks * per_slice, t.mt, t.nt);
   const int per = (nkb + nsplit - 1) / nsplit;

@@ -209,7 +209,7 @@ def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
     mark("start")
     # dW, each band's tiles stored straight into its owner's receive slot
     st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), g.data_ptr(), ex.band_out,
-                             ex.world, ex.band_rows, ws.data_ptr(), ws.numel(), stream)
+                             ex.world, ex.band_rows, (ex.rank + 1) % ex.world, ws.data_ptr(), ws.numel(), stream)
     _lib.check(st, "gh_lce_dw_peers")
     mark("dw_gemm")
     ex.barrier()  # every rank's slot of my band has arrived

@@ -292,7 +292,7 @@ def linear_cross_entropy_grads_from(ws: Tensor, inputs: Tensor, weight: Tensor, 
     gw = torch.empty((V, D), dtype=weight.dtype, device=dev)
     band = (ctypes.c_void_p * 1)(gw.data_ptr())  # one band: this GPU's own gradient
     st = lib.gh_lce_dw_peers(x.data_ptr(), B, D, V, code, chunk, int(fp32_accum), _lib.ptr(g), band, 1,
-                             -(-V // 256) * 256, ws.data_ptr(), ws.numel(), stream)
+                             -(-V // 256) * 256, 0, ws.data_ptr(), ws.numel(), stream)
     _lib.check(st, "linear_cross_entropy dW")
     gi = torch.empty((B, D), dtype=inputs.dtype, device=dev)
     st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, _lib.ptr(g),

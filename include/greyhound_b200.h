@@ -238,11 +238,14 @@ GH_API int gh_lce_dh_last_chunk(const void* W, int64_t N, int64_t D, int64_t V, 
  * memory (a CUDA IPC mapping): the data-parallel caller gives each rank's
  * receive slot, so the GEMM's epilogue performs the scatter of a
  * reduce-scatter of the weight gradient (no counterpart in the reference,
- * which is single-device). The kernel ends with a system-scope fence, so
+ * which is single-device). The GEMM computes band first_band's tiles first
+ * and wraps around (each rank passes its own index, so the ranks' stores
+ * go to different owners at any moment). The kernel ends with a
+ * system-scope fence, so
  * once it has completed the stores are visible to the owners. */
 GH_API int gh_lce_dw_peers(const void* H, int64_t N, int64_t D, int64_t V, int dtype,
                            int64_t chunk_rows, int fp32_grad_weight_accum, const float* scale,
-                           void* const* band_out, int nbands, int64_t band_rows,
+                           void* const* band_out, int nbands, int64_t band_rows, int first_band,
                            void* workspace, size_t workspace_bytes, void* stream);
 
 /* out0[r, c] (and out1[r, c] when out1 != NULL) = sum over s < nslots of
