@@ -315,8 +315,8 @@ def bench_lce(args, rank, world, local):
                  "share_of_step": tot_ms / (ms * args.steps)}
             if cls.startswith("gemm_") and cls != "gemm_other":
                 k["tflops"] = gemm_flops / (per * 1e-3) / 1e12
-            if cls == "dlogits":
-                k["gbs"] = 2 * N * V * 2 / (per * 1e-3) / 1e9
+            if cls == "glue":  # the small kernels between the GEMMs (q fix-up, target column, alpha * H)
+                k["note"] = "q fix-up, target column, alpha*H (or the logits -> dlogits pass when q mode is off)"
             kernels[cls] = k
     gemms = [c for c in kernels if c.startswith("gemm_") and c != "gemm_other"]
     dom = max(gemms, key=lambda c: kernels[c]["share_of_step"], default=None)

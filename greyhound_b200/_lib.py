@@ -97,7 +97,7 @@ SIGNATURES: dict[str, tuple] = {
 GH_LCE_DEFER_LAST_DH = 1
 GH_LCE_KEEP_DW_OPERAND = 2
 GH_LCE_GRADS_LATER = 4
-PROF_CLASSES = ("gemm_logits_ce", "gemm_dw", "gemm_dh", "dlogits", "rows", "gemm_other")
+PROF_CLASSES = ("gemm_logits_ce", "gemm_dw", "gemm_dh", "glue", "rows", "gemm_other")
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

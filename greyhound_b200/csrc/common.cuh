@@ -33,7 +33,7 @@ enum ProfClass {
   PROF_GEMM_LOGITS_CE = 0,  // logits GEMM with the fused CE epilogue
   PROF_GEMM_DW = 1,
   PROF_GEMM_DH = 2,
-  PROF_DLOGITS = 3,
+  PROF_DLOGITS = 3,         // the small kernels between the GEMMs (q fix-up, alpha * H, or the dlogits pass)
   PROF_ROWS = 4,            // standalone CE / SLS row kernels
   PROF_GEMM_OTHER = 5,
   PROF_NUM = 6
