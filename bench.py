@@ -42,10 +42,11 @@ METRIC = "linear-CE fwd+bwd tokens/s, Llama-3-8B head; % bf16 TC peak @1/2/4/8 G
 # DRAM bytes (read + write) per launch from one ncu capture of each kernel class
 # at the bench workload (one-pass ncu capture of each GEMM class); None if not captured.
 TRAFFIC_BYTES_PER_LAUNCH: dict = {
-    # Llama-3-8B head, one chunk: DRAM read + write per launch
-    "gemm_logits_ce": 4.15e9 + 2.11e9,
-    "gemm_dw": 18.28e9 + 1.04e9,
-    "gemm_dh": 21.68e9 + 0.063e9,
+    # Llama-3-8B head, one chunk, q-store pipeline: DRAM read + write per
+    # launch (profiles/tc_gemm_cfg3_traffic.md)
+    "gemm_logits_ce": 9.471e9 + 2.116e9,
+    "gemm_dw": 15.047e9 + 1.035e9,
+    "gemm_dh": 17.082e9 + 0.124e9,
 }
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
