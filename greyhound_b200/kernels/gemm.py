@@ -14,7 +14,7 @@ from torch import Tensor
 
 from greyhound_b200 import _lib
 
-__all__ = ["gemm_nt", "supports"]
+__all__ = ["gemm_nt", "gemm_nt_fp32", "supports"]
 
 
 def _operand(t: Tensor) -> tuple[Tensor, int, int]:
@@ -74,3 +74,39 @@ def gemm_nt(
     )
     _lib.check(st, "gemm_nt")
     return out
+
+
+def _split3(t: Tensor, kp: int) -> tuple[Tensor, Tensor, Tensor]:
+    """fp32 [R, K] -> three bf16 [R, kp] pieces t1 + t2 + t3 = t (to ~2^-24
+    relative; zero padding from K to kp)."""
+    t = t.float()
+    t1 = t.bfloat16()
+    r = t - t1.float()
+    t2 = r.bfloat16()
+    t3 = (r - t2.float()).bfloat16()
+    if kp != t.shape[1]:
+        pad = lambda u: torch.nn.functional.pad(u, (0, kp - t.shape[1]))  # noqa: E731
+        t1, t2, t3 = pad(t1), pad(t2), pad(t3)
+    return t1, t2, t3
+
+
+def gemm_nt_fp32(a: Tensor, b: Tensor, out: Tensor | None = None, addend: Tensor | None = None) -> Tensor:
+    """fp32 ``a @ b.T (+ addend)`` on the bf16 tcgen05 GEMM, to about fp32
+    accuracy: each operand is split into three bf16 pieces (x = x1 + x2 + x3)
+    and the six products whose magnitude reaches 2^-24 of the result
+    (a1b1, a1b2, a2b1, a1b3, a2b2, a3b1) are summed in the GEMM's fp32
+    accumulator as one GEMM over a 6x longer K (the pieces concatenated along
+    K). This is the usual split-precision emulation of single precision on
+    lower-precision tensor cores; it replaces the cuBLAS SGEMMs of the fp32
+    operands (PyTorch's default fp32 matmul does not round to TF32, so
+    neither does this)."""
+    if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[1]:
+        raise ValueError(f"gemm_nt_fp32 expects A [M, K] and B [N, K], got {tuple(a.shape)} and {tuple(b.shape)}")
+    M, K = a.shape
+    kp = -(-K // 8) * 8
+    a1, a2, a3 = _split3(a, kp)
+    b1, b2, b3 = _split3(b, kp)
+    A = torch.cat([a1, a1, a2, a1, a2, a3], dim=1)
+    B = torch.cat([b1, b2, b1, b3, b2, b1], dim=1)
+    del a1, a2, a3, b1, b2, b3
+    return gemm_nt(A, B, out_dtype=torch.float32, out=out, addend=addend)

@@ -174,7 +174,10 @@ def linear_cross_entropy_with_grad(
     if _tc_ok(inputs, weight):
         return _tc_lce(inputs, weight, target, z_loss_multiplier, fp32_grad_weight_accum, ignore_index,
                        mean_reduction, grad_scale, True, grad_weight_hook)
-    # fp32 operands: cuBLAS GEMMs around the CE row kernel
+    # fp32 operands: the CE row kernel between fp32 GEMMs emulated on the
+    # bf16 tcgen05 GEMM (kernels/gemm.py:gemm_nt_fp32)
+    from greyhound_b200.kernels.gemm import gemm_nt_fp32
+
     B, D = inputs.shape
     V = weight.shape[1]
     chunk = chunk_size_for(B, D, V, inputs.element_size())
@@ -193,15 +196,18 @@ def linear_cross_entropy_with_grad(
     for s in range(0, B, chunk):
         e = min(s + chunk, B)
         x = inputs[s:e]
-        logits = x @ weight
+        logits = gemm_nt_fp32(x, weight.T).to(inputs.dtype)
         c, z, n = cross_entropy_with_grad(
             logits, target[s:e], z_loss_multiplier, ignore_index, logits, grad_scale=scale
         )
         ce_sum += c
         z_sum += z
         n_valid += n
-        grad_input[s:e] = logits @ weight.T
-        torch.addmm(grad_weight_acc, logits.T, x, out=grad_weight_acc, out_dtype=acc_dtype)
+        grad_input[s:e] = gemm_nt_fp32(logits, weight).to(inputs.dtype)
+        if acc_dtype == torch.float32:
+            gemm_nt_fp32(logits.T, x.T, out=grad_weight_acc, addend=grad_weight_acc)
+        else:
+            grad_weight_acc += gemm_nt_fp32(logits.T, x.T).to(acc_dtype)
     grad_weight_vd = grad_weight_acc.to(weight.dtype)
     if grad_weight_hook is not None:
         work = grad_weight_hook(grad_weight_vd)
@@ -315,6 +321,8 @@ def linear_cross_entropy_loss(
         ce, z, n, _, _ = _tc_lce(inputs, weight, target, z_loss_multiplier, True, ignore_index,
                                  False, None, False)
         return ce, z, n
+    from greyhound_b200.kernels.gemm import gemm_nt_fp32
+
     B, D = inputs.shape
     V = weight.shape[1]
     chunk = chunk_size_for(B, D, V, inputs.element_size())
@@ -325,7 +333,7 @@ def linear_cross_entropy_loss(
     n_valid = torch.zeros((), dtype=torch.float32, device=dev)
     for s in range(0, B, chunk):
         e = min(s + chunk, B)
-        logits = inputs[s:e] @ weight
+        logits = gemm_nt_fp32(inputs[s:e], weight.T).to(inputs.dtype)
         c, z, n = cross_entropy_with_grad(logits, target[s:e], z_loss_multiplier, ignore_index, None)
         ce_sum += c
         z_sum += z
@@ -361,10 +369,11 @@ def vocab_shard_stats(
                                     code, stats.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_of(x))
         _lib.check(st, "vocab_shard_stats")
         return stats, ("tc", ws, x, w)
-    # fp32 operands: cuBLAS GEMM + the CE row kernel for the shard logsumexp
+    # fp32 operands: emulated fp32 GEMM + the CE row kernel for the shard logsumexp
     from greyhound_b200.kernels.cross_entropy import cross_entropy_with_grad as _ce
+    from greyhound_b200.kernels.gemm import gemm_nt_fp32
 
-    logits = inputs @ weight_shard.T
+    logits = gemm_nt_fp32(inputs, weight_shard).to(inputs.dtype)
     lse = torch.empty(rows, dtype=torch.float32, device=dev)
     never = torch.full_like(target, -(1 << 62))
     _ce(logits, never, 0.0, -(1 << 62), None, lse_out=lse)
@@ -434,9 +443,11 @@ def vocab_shard_grads(
         sc.data_ptr(), _lib.stream_of(logits),
     )
     _lib.check(st, "gh_logits_grad")
-    gi = logits @ weight_shard
+    from greyhound_b200.kernels.gemm import gemm_nt_fp32
+
+    gi = gemm_nt_fp32(logits, weight_shard.T).to(inputs.dtype)
     work = grad_input_hook(gi) if grad_input_hook is not None else None
-    gw = logits.T @ inputs
+    gw = gemm_nt_fp32(logits.T, inputs.T).to(inputs.dtype)
     if work is not None:
         work.wait()
     return gi, gw

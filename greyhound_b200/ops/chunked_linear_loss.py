@@ -16,7 +16,7 @@ from collections.abc import Callable
 import torch
 from torch import Tensor
 
-from greyhound_b200.kernels.gemm import gemm_nt
+from greyhound_b200.kernels.gemm import gemm_nt, gemm_nt_fp32
 from greyhound_b200.kernels.linear_cross_entropy import chunk_size_for
 from greyhound_b200.ops.scale import scale_by
 
@@ -59,7 +59,14 @@ def _logits(input_chunk: Tensor, weight: Tensor) -> Tensor:
     """``input_chunk @ weight`` ([D, V] operand): tcgen05 GEMM for bf16/fp16."""
     if _tc_ok(input_chunk, weight):
         return gemm_nt(input_chunk, weight.T)
+    if _fp32_ok(input_chunk, weight):
+        return gemm_nt_fp32(input_chunk, weight.T)
     return input_chunk @ weight
+
+
+def _fp32_ok(*ts: Tensor) -> bool:
+    """fp32 CUDA operands: the fp32 GEMMs emulated on the bf16 tcgen05 GEMM."""
+    return all(t.is_cuda and t.dtype == torch.float32 for t in ts)
 
 
 def _padded_grad(grad_logits: Tensor, dtype: torch.dtype) -> Tensor:
@@ -109,6 +116,10 @@ def _chunked_linear_loss_with_grad(
             gemm_nt(g, weight, out=grad_input[start:end])  # dlogits [C,V] . W [V,D]
             gemm_nt(g.T, input_chunk.T, out=grad_weight_accum,
                     addend=None if start == 0 else grad_weight_accum)
+        elif _fp32_ok(inputs, weight) and acc_dtype == torch.float32:
+            g = grad_logits.float()
+            grad_input[start:end] = gemm_nt_fp32(g, weight)
+            gemm_nt_fp32(input_chunk.T, g.T, out=grad_weight_accum, addend=grad_weight_accum)
         else:
             grad_input[start:end] = grad_logits @ weight.T
             torch.addmm(
