@@ -91,15 +91,16 @@ def _split3(t: Tensor, kp: int) -> tuple[Tensor, Tensor, Tensor]:
 
 
 def gemm_nt_fp32(a: Tensor, b: Tensor, out: Tensor | None = None, addend: Tensor | None = None) -> Tensor:
-    """fp32 ``a @ b.T (+ addend)`` on the bf16 tcgen05 GEMM, to about fp32
-    accuracy: each operand is split into three bf16 pieces (x = x1 + x2 + x3)
-    and the six products whose magnitude reaches 2^-24 of the result
-    (a1b1, a1b2, a2b1, a1b3, a2b2, a3b1) are summed in the GEMM's fp32
-    accumulator as one GEMM over a 6x longer K (the pieces concatenated along
-    K). This is the usual split-precision emulation of single precision on
-    lower-precision tensor cores; it replaces the cuBLAS SGEMMs of the fp32
-    operands (PyTorch's default fp32 matmul does not round to TF32, so
-    neither does this)."""
+    """fp32 ``a @ b.T (+ addend)`` on the bf16 tcgen05 GEMM: each operand is
+    split into three bf16 pieces (x = x1 + x2 + x3, 24 significand bits) and
+    the six products whose magnitude reaches 2^-24 of the result (a1b1, a1b2,
+    a2b1, a1b3, a2b2, a3b1) are summed in the GEMM's fp32 accumulator as one
+    GEMM over a 6x longer K (the pieces concatenated along K): the usual
+    split-precision emulation of single precision on lower-precision tensor
+    cores. Measured error against fp64: 0.6-4.5e-5 of max|C| for K up to
+    4096 (the tensor cores' accumulation dominates), where cuBLAS SGEMM gives
+    0.3-3e-6 and a TF32 GEMM about 1e-3 (PyTorch's default fp32 matmul does
+    not round to TF32). It replaces the cuBLAS SGEMMs of the fp32 operands."""
     if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[1]:
         raise ValueError(f"gemm_nt_fp32 expects A [M, K] and B [N, K], got {tuple(a.shape)} and {tuple(b.shape)}")
     M, K = a.shape
