@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
 
@@ -269,6 +270,12 @@ struct Hints {
 // and 7-9 % less time. The dW GEMM keeps the n-fastest order (other orders
 // and groupings read more).
 constexpr int kLogitsGroup = 16;
+// GREYHOUND_B200_LOGITS_GROUP overrides it (tuning sweeps)
+inline int logits_group() {
+  const char* e = getenv("GREYHOUND_B200_LOGITS_GROUP");
+  const int g = e && *e ? atoi(e) : kLogitsGroup;
+  return g >= 1 ? g : kLogitsGroup;
+}
 // dW / logits-style GEMMs: the 2 GB dlogits (or W) stream must not evict the
 // small H operand that every tile re-reads.
 constexpr Hints kStreamA_KeepB{1, 2, 1};
@@ -346,6 +353,16 @@ int run_gemm(int dtype, const Operand& A, const Operand& B, int64_t M, int64_t N
   p.out2 = tl.ksplit > 1 ? split_out : nullptr;
   p.raster = raster;
   p.group = 1;
+  // tile-order override for the gradient GEMMs, "raster,group"
+  // (GREYHOUND_B200_DW_ORDER / GREYHOUND_B200_DH_ORDER; tuning sweeps)
+  if (prof_class == PROF_GEMM_DW || prof_class == PROF_GEMM_DH) {
+    const char* e = getenv(prof_class == PROF_GEMM_DW ? "GREYHOUND_B200_DW_ORDER" : "GREYHOUND_B200_DH_ORDER");
+    int r = -1, g = 1;
+    if (e && *e && sscanf(e, "%d,%d", &r, &g) >= 1 && r >= 0 && r <= 3 && g >= 1) {
+      p.raster = r;
+      p.group = g;
+    }
+  }
   p.out = out;
   p.ldo = ldo;
   const int oelt = elt_size(out_dtype);
@@ -693,7 +710,7 @@ int lce_run(const void* H, const void* W, const int64_t* target, int64_t N, int6
       gemm::Params p{};
       set_tiles(p, rows, V, D, pair, nsub);
       p.raster = 2;
-      p.group = kLogitsGroup;
+      p.group = logits_group();
       p.out = with_grad ? logits : nullptr;  // forward only: statistics, no logits
       p.ldo = L.ldl;
       p.vec_ok = ((L.ldl * (int64_t)sizeof(T)) & 15) == 0;
