@@ -20,6 +20,7 @@
 //     the label logit, a second kernel merges them and writes the gradient.
 // Per-row loss terms go to workspace arrays; one single-CTA kernel sums them
 // in a fixed order, so results are bit-reproducible run to run.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -313,8 +314,20 @@ int launch_ce(const void* logits, void* dlogits, const int64_t* labels, int64_t 
       int64_t grid = rows;
       const int64_t cap = (int64_t)num_sms() * 2 * 64;
       if (grid > cap) grid = cap;
-      ce_fused_kernel<T, kFusedThreads, kUnroll><<<(unsigned)grid, kFusedThreads, 0, st>>>(
-          x, y, labels, rows, V, zmul, ignore, sp, row_ce, row_z, lse_out, status);
+      // 32-byte vectors in flight per thread: 3 (measured at cfg2: 2 -> 5.02,
+      // 3 -> 5.19, 4 -> 4.84 TB/s, the last spilling registers);
+      // GREYHOUND_B200_CE_UNROLL = 2 or 4 selects the others
+      const char* ue = getenv("GREYHOUND_B200_CE_UNROLL");
+      const int un = ue && *ue ? atoi(ue) : 3;
+      if (un == 3)
+        ce_fused_kernel<T, kFusedThreads, 3><<<(unsigned)grid, kFusedThreads, 0, st>>>(
+            x, y, labels, rows, V, zmul, ignore, sp, row_ce, row_z, lse_out, status);
+      else if (un == 4)
+        ce_fused_kernel<T, kFusedThreads, 4><<<(unsigned)grid, kFusedThreads, 0, st>>>(
+            x, y, labels, rows, V, zmul, ignore, sp, row_ce, row_z, lse_out, status);
+      else
+        ce_fused_kernel<T, kFusedThreads, kUnroll><<<(unsigned)grid, kFusedThreads, 0, st>>>(
+            x, y, labels, rows, V, zmul, ignore, sp, row_ce, row_z, lse_out, status);
       ++launches;
     } else {
       float2* part = reinterpret_cast<float2*>(ws + w.part);
