@@ -1,4 +1,6 @@
-"""Test marks, as in src/greyhound/testing.py:4-11."""
+"""Test marks: the reference's `has_cuda` / `GPU_MARKS` / `requires_gpu`
+(src/greyhound/testing.py:1-11) kept as they are there, because the
+reference-style tests are written against exactly these names and marks."""
 
 import pytest
 import torch
