@@ -109,3 +109,20 @@ def test_dead_rank_is_detected_not_hung():
     out = _run(W.dead_rank_worker, _data(), timeout=120)
     assert out[1][1] == "left"
     assert out[0][1] == "detected", out
+
+
+def test_band_exchange_band_arithmetic():
+    """Row bands of the fused weight-gradient reduce-scatter: multiples of the
+    256-row GEMM tile that cover the vocabulary, every rank owning a
+    non-empty band (else the NCCL all-reduce path is taken)."""
+    from greyhound_b200.distributed import _band_rows
+
+    for V in (1000, 30011, 32000, 128256, 151936):
+        for world in (2, 3, 4, 8):
+            b = _band_rows(V, world)
+            assert b % 256 == 0 and world * b >= V and b - 256 < -(-V // world)
+            last = V - (world - 1) * b
+            if last > 0:
+                assert last <= b
+    assert _band_rows(128256, 8) == 16128
+    assert 7 * _band_rows(1000, 8) >= 1000  # too small a vocabulary: no band for the last ranks
