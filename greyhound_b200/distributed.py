@@ -156,21 +156,57 @@ DP_PHASES: list = []  # per backward: [(phase, CUDA event)], when _DP_TIMING
 
 
 def dp_phase_summary() -> dict:
-    """Mean ms of each band-exchange phase (from the previous mark) over the
-    recorded backwards; synchronises. Copies are measured from barrier2."""
+    """Mean ms of each band-exchange phase over the recorded backwards;
+    synchronises. Each phase is measured from the mark it follows in stream
+    order (the dH GEMM from the end of dW when it overlaps the exchange)."""
     torch.cuda.synchronize()
     acc: dict = {}
-    for marks in DP_PHASES:
+    for overlap, marks in DP_PHASES:
         d = dict(marks)
-        prev = None
+        ref = {"dw_gemm": "start", "barrier1": "dw_gemm", "sum_slots": "barrier1", "barrier2": "sum_slots",
+               "copies_done": "barrier2", "dh_gemm": "dw_gemm" if overlap else "copies_done",
+               "joined": "dh_gemm"}
+        if not overlap:
+            ref["dh_gemm"] = "barrier2"
         for name, ev in marks:
-            if prev is not None:
-                ref = d["barrier2"] if name == "copies_done" else prev
-                acc.setdefault(name, []).append(ref.elapsed_time(ev))
-            if name != "copies_done":
-                prev = ev
+            if name in ref and ref[name] in d:
+                acc.setdefault(name, []).append(d[ref[name]].elapsed_time(ev))
     DP_PHASES.clear()
     return {k: sum(v) / len(v) for k, v in acc.items()}
+
+
+def _dp_overlap_sms() -> int:
+    """SMs left to the weight-gradient exchange while the dH GEMM runs
+    (GREYHOUND_B200_DP_OVERLAP_SMS; 0 runs the exchange before dH)."""
+    import os
+
+    return max(0, int(os.environ.get("GREYHOUND_B200_DP_OVERLAP_SMS", "8")))
+
+
+def _exchange(ex, lib, gw, D, code, me, elt, cs, mark):
+    """Barrier, fixed-order sum of this rank's band, barrier, and the copy-
+    engine pulls of the other bands (on ``cs``); the stream-ordered part runs
+    on the current stream."""
+    from greyhound_b200 import _lib
+
+    ex.barrier()  # every rank's slot of my band has arrived
+    mark("barrier1", torch.cuda.current_stream())
+    st = lib.gh_sum_slots(ex.recv.data_ptr(), ex.world, ex.band_rows * D, ex.rows_of(me), D, D, code,
+                          ex.shard.data_ptr(), gw[me * ex.band_rows:].data_ptr(),
+                          torch.cuda.current_stream().cuda_stream)
+    _lib.check(st, "gh_sum_slots")
+    mark("sum_slots", torch.cuda.current_stream())
+    ex.barrier()  # every rank's reduced band is ready
+    mark("barrier2", torch.cuda.current_stream())
+    ready = torch.cuda.Event()
+    ready.record()
+    cs.wait_event(ready)
+    for r in range(ex.world):
+        if r != me:
+            st = lib.gh_memcpy_async(gw[r * ex.band_rows:].data_ptr(), ex.shard_src[r], ex.rows_of(r) * D * elt,
+                                     cs.cuda_stream)
+            _lib.check(st, "gh_memcpy_async")
+    mark("copies_done", cs)
 
 
 def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
@@ -212,36 +248,33 @@ def _band_exchange_grads(ws, inputs, weight_dv, grad_output, fp32_accum, group):
                              ex.world, ex.band_rows, (ex.rank + 1) % ex.world, ws.data_ptr(), ws.numel(), stream)
     _lib.check(st, "gh_lce_dw_peers")
     mark("dw_gemm")
-    ex.barrier()  # every rank's slot of my band has arrived
-    mark("barrier1")
     me = ex.rank
-    st = lib.gh_sum_slots(ex.recv.data_ptr(), ex.world, ex.band_rows * D, ex.rows_of(me), D, D, code,
-                          ex.shard.data_ptr(), gw[me * ex.band_rows:].data_ptr(), stream)
-    _lib.check(st, "gh_sum_slots")
-    mark("sum_slots")
-    ex.barrier()  # every rank's reduced band is ready
-    mark("barrier2")
-    ready = torch.cuda.Event()
-    ready.record()
     cs = ex.copy_stream
-    cs.wait_event(ready)
     elt = gw.element_size()
-    for r in range(ex.world):
-        if r != me:
-            st = lib.gh_memcpy_async(gw[r * ex.band_rows:].data_ptr(), ex.shard_src[r], ex.rows_of(r) * D * elt,
-                                     cs.cuda_stream)
-            _lib.check(st, "gh_memcpy_async")
-    mark("copies_done", cs)
-    # the input gradient on all SMs while the copy engines move the bands
-    st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, g.data_ptr(),
-                                  gi.data_ptr(), ws.data_ptr(), ws.numel(), 0, stream)
+    reserve = _dp_overlap_sms()
+    if reserve > 0:
+        # the exchange (barriers, slot sum, band copies) on its own stream
+        # and `reserve` SMs, concurrent with the dH GEMM on the others
+        ready = torch.cuda.Event()
+        ready.record()
+        cs.wait_event(ready)
+        with torch.cuda.stream(cs):
+            _exchange(ex, lib, gw, D, code, me, elt, cs, mark)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, g.data_ptr(),
+                                      gi.data_ptr(), ws.data_ptr(), ws.numel(), max(2, sms - reserve), stream)
+    else:
+        _exchange(ex, lib, gw, D, code, me, elt, cs, mark)
+        # the input gradient on all SMs while the copy engines move the bands
+        st = lib.gh_lce_dh_last_chunk(w.data_ptr(), B, D, V, code, chunk, int(fp32_accum), 0, -1, g.data_ptr(),
+                                      gi.data_ptr(), ws.data_ptr(), ws.numel(), 0, stream)
     _lib.check(st, "linear_cross_entropy dH")
     mark("dh_gemm")
     torch.cuda.current_stream(dev).wait_stream(cs)
     mark("joined")
     gw.record_stream(cs)
     if _DP_TIMING:
-        DP_PHASES.append(marks)
+        DP_PHASES.append((reserve > 0, marks))
     return gi, gw.T
 
 
