@@ -177,10 +177,12 @@ def dp_phase_summary() -> dict:
 
 def _dp_overlap_sms() -> int:
     """SMs left to the weight-gradient exchange while the dH GEMM runs
-    (GREYHOUND_B200_DP_OVERLAP_SMS; 0 runs the exchange before dH)."""
+    (GREYHOUND_B200_DP_OVERLAP_SMS, default 0: the exchange runs before dH).
+    Measured at 2 GPUs with 8 SMs: the slot sum slows from 0.42 to 5.0 ms
+    and dH by 0.5 ms, for the same step time (20.41 against 20.45 ms)."""
     import os
 
-    return max(0, int(os.environ.get("GREYHOUND_B200_DP_OVERLAP_SMS", "8")))
+    return max(0, int(os.environ.get("GREYHOUND_B200_DP_OVERLAP_SMS", "0")))
 
 
 def _exchange(ex, lib, gw, D, code, me, elt, cs, mark):
